@@ -1,0 +1,378 @@
+"""Benchmark of the attention hot path (prologue + attention, 28 layers).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One step = one pass of the hot path over one micro-batch: for each of the 28
+layers, the fused Q/K RMSNorm + RoPE prologue and the causal/sparse GQA
+attention (the two runs Qwen3ExecutionPlan encodes per layer,
+src/webgpu/model.ts:94-95), each layer with its own seeded inputs.
+
+Multi-GPU (torchrun, one process per GPU): requests are independent, so
+every rank runs its own micro-batch of the workload (weak scaling) with no
+collective on the hot path; the barrier + max-over-ranks timing only frame
+the measurement. ``value`` = tokens of all ranks / max step time.
+
+``--impl reference``: the reference's hot path exists only as WGSL for a
+browser WebGPU (unavailable on this box), so this arm times the CPU oracle
+(a C/OpenMP restatement of the same math) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+PKG = "qwen3-embedding-webgpu-prepacked_b200"
+DEFAULT_WORKLOAD = "c5_16x5000_sparse"
+METRIC = "prefill attention tokens/s (GQA 16/8x128, 28 layers)"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        try:
+            p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                  "--format=csv,noheader,nounits", "-lms", "200"],
+                                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return
+        while not self._stop.is_set():
+            line = p.stdout.readline()
+            if not line:
+                break
+            self.rows.append([x.strip() for x in line.split(",")])
+        p.terminate()
+        try:
+            p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            p.kill()
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if len(r) > 3 + i and r[3 + i] == "Active"})
+        loaded = sorted(sm)[len(sm) // 4:] if sm else []
+        return {"sm_mhz": float(np.median(loaded)) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def dist_setup(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        import torch
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def cpu_baseline(pkg, workload, seconds_budget=20.0):
+    """The CPU oracle (C/OpenMP restatement, all host threads) on a bounded
+    sample of the workload: one request of the workload through one layer
+    (prologue + attention over all its rows), scaled to tokens/s through 28
+    layers."""
+    from oracle import oracle
+    L = int(max(workload.lengths))
+    cu = [0, L]
+    qkv, qw, kw = pkg.workloads.host_layer_inputs(L, seed=1)
+    sparse_mode = workload.mode
+    reps, elapsed = 0, 0.0
+    t0 = time.perf_counter()
+    while True:
+        q, k = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+        oracle.c_attention(q.astype(np.float16), k.astype(np.float16), qkv, 4096, 3072, cu,
+                           sparse_mode if sparse_mode else 0)
+        reps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed > seconds_budget / 4 or reps >= 3:
+            break
+    per_layer = elapsed / reps
+    value = L / (per_layer * workload.layers)
+    return {"value": value, "unit": UNIT, "cores": oracle.threads(), "kind": "port",
+            "sample": f"1 request x {L} tokens x 1 layer (prologue + attention, all rows), "
+                      f"{reps} rep(s), scaled to {workload.layers} layers"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the CPU oracle on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    pkg = importlib.import_module(PKG)
+    from oracle import oracle
+    w = pkg.workloads.WORKLOADS[args.workload]
+    # a bounded sample per step: one request through one layer, all rows
+    L = int(max(w.lengths))
+    qkv, qw, kw = pkg.workloads.host_layer_inputs(L, seed=1)
+    cu = [0, L]
+
+    def step():
+        q, k = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+        oracle.c_attention(q.astype(np.float16), k.astype(np.float16), qkv, 4096, 3072, cu,
+                           w.mode)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = L / (dt * w.layers)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": w.name, "requests": len(w.lengths), "seq_len": L,
+                   "layers": w.layers, "mode": w.mode,
+                   "note": "reference WGSL/WebGPU path unavailable on this box; CPU oracle "
+                           "(C/OpenMP restatement of src/webgpu/ops.ts) timed instead"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.threads(), "kind": "port",
+                         "sample": f"1 request x {L} tokens x 1 layer per step, scaled to "
+                                   f"{w.layers} layers"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    import torch
+    pkg = importlib.import_module(PKG)
+    attn = pkg.attention
+    lib = pkg._lib.load()
+    w = pkg.workloads.WORKLOADS[args.workload]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    ctx = attn.Context.for_device(local)
+    cu = w.cu_seqlens()
+    cu_c = pkg._lib.cu_array(cu)
+    T = w.tokens
+    L = w.layers
+
+    # inputs resident in HBM: one qkv activation per layer (each > L2, so
+    # consecutive layers never hit in L2), per-layer norm weights
+    layers = [pkg.workloads.device_layer_inputs(T, seed=1000 * rank + l, device=dev)
+              for l in range(L)]
+    q_buf = torch.empty(T, 16, 128, dtype=torch.float16, device=dev)
+    k_buf = torch.empty(T, 8, 128, dtype=torch.float16, device=dev)
+    out = torch.empty(T, 16, 128, dtype=torch.float16, device=dev)
+    stream = torch.cuda.Stream(dev)
+    s = stream.cuda_stream
+    P = attn._ptr
+
+    def layer_calls(qkv, qw, kw, ev=None):
+        st = lib.qwa_qk_norm_rope(ctx.handle, P(qkv), 4096, P(qw), P(kw), P(q_buf), P(k_buf),
+                                  cu_c, len(cu) - 1, 1e-6, 1e6, None, s)
+        if st:
+            pkg._lib.check(st, ctx.handle)
+        if ev is not None:
+            ev[0].record(stream)
+        st = lib.qwa_attention(ctx.handle, P(q_buf), P(k_buf), P(qkv), 4096, 3072, P(out), cu_c,
+                               len(cu) - 1, w.mode, 176, 432, s)
+        if st:
+            pkg._lib.check(st, ctx.handle)
+        if ev is not None:
+            ev[1].record(stream)
+
+    def step(evs=None):
+        for l, (qkv, qw, kw) in enumerate(layers):
+            layer_calls(qkv, qw, kw, evs[l] if evs is not None else None)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    ctx.check(stream)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    # timed region: K steps, events around each attention launch as well
+    ev_layer = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(L)]
+                for _ in range(args.steps)]
+    ev_pro_start = [[torch.cuda.Event(enable_timing=True) for _ in range(L)]
+                    for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for kstep in range(args.steps):
+            for l, (qkv, qw, kw) in enumerate(layers):
+                ev_pro_start[kstep][l].record(stream)
+                layer_calls(qkv, qw, kw, ev_layer[kstep][l])
+        end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ctx.check(stream)
+    ms = start.elapsed_time(end) / args.steps
+    attn_ms = [ev_layer[k][l][0].elapsed_time(ev_layer[k][l][1])
+               for k in range(args.steps) for l in range(L)]
+    pro_ms = [ev_pro_start[k][l].elapsed_time(ev_layer[k][l][0])
+              for k in range(args.steps) for l in range(L)]
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # end to end through the C ABI with host buffers: every layer's qkv
+    # crosses host->device from pinned memory, the layer output comes back
+    e2e = None
+    if not args.no_e2e:
+        host_in = [torch.empty(T, 4096, dtype=torch.float16).pin_memory() for _ in range(2)]
+        for h in host_in:
+            h.copy_(layers[0][0].cpu())
+        host_out = torch.empty(T, 16, 128, dtype=torch.float16).pin_memory()
+        dev_in = torch.empty(T, 4096, dtype=torch.float16, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def e2e_step():
+            for l in range(L):
+                dev_in.copy_(host_in[l % 2], non_blocking=True)
+                layer_calls(dev_in, layers[l][1], layers[l][2])
+                host_out.copy_(out, non_blocking=True)
+
+        with torch.cuda.stream(stream):
+            e2e_step()
+            torch.cuda.synchronize()
+            barrier()
+            e0.record(stream)
+            for _ in range(args.e2e_steps):
+                e2e_step()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": T * 4096 * 2 * L,
+               "d2h_bytes_per_step": T * 2048 * 2 * L, "ms_per_step": e2e_ms}
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+
+    peaks, src = measured_peaks()
+    pairs, tiles = attn.attention_work(cu, w.mode)
+    flop_per_launch = 8192.0 * pairs
+    attn_avg = float(np.mean(attn_ms))
+    pro_avg = float(np.mean(pro_ms))
+    achieved_tflops = flop_per_launch / (attn_avg * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
+    pro_bytes = T * (2048 + 1024) * 2 * 2  # read q,k columns; write q,k
+    attn_bytes = T * 12288  # algorithmic bytes of the hot path per token
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "attention_traffic.json")
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            tinfo = json.load(f).get(w.name)
+        if tinfo:
+            traffic = tinfo["bytes_per_launch"]
+    line = {
+        "metric": METRIC, "value": world * T / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) qkv per layer, weights 1+N(0,0.02))",
+        "config": {"workload": w.name, "requests_per_rank": len(w.lengths),
+                   "seq_len": int(max(w.lengths)), "tokens_per_rank": T, "layers": L,
+                   "mode": ["auto(sparse<=8192)", "full", "sparse"][w.mode],
+                   "global_batch": world * len(w.lengths), "parallelism": f"dp{world} (by request)",
+                   "l2": "inputs larger than L2 (one 655 MB qkv per layer)"},
+        "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved_tflops / peak, "traffic": traffic,
+                     "kernel": "attention_kernel", "flop_per_launch": flop_per_launch,
+                     "avg_launch_ms": attn_avg,
+                     "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a "
+                                    f"{L}-layer step)"},
+        "prologue": {"avg_launch_ms": pro_avg, "bytes_per_launch": pro_bytes,
+                     "achieved_gbs": pro_bytes / (pro_avg * 1e-3) / 1e9,
+                     "peak_gbs": peaks["hbm_gbs"],
+                     "frac": pro_bytes / (pro_avg * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        "attention_share_of_step": float(np.sum(attn_ms) / args.steps / ms),
+        "algorithmic_bytes_per_token_layer": 12288, "hot_path_bytes_per_step": attn_bytes * L,
+        "gpu_launches": 2 * L * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if e2e:
+        line["e2e"] = e2e
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(pkg, w)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

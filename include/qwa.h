@@ -1,0 +1,155 @@
+/*
+ * qwa.h -- C ABI of the B200 (sm_100a) attention hot path for
+ * Qwen3-Embedding-0.6B-shaped layers: fused per-head Q/K RMSNorm + RoPE,
+ * and causal / sparse (prefix + local window) GQA prefill attention over
+ * ragged micro-batches.
+ *
+ * Shapes are fixed by the model: 16 query heads, 8 key/value heads,
+ * head_dim 128, f16 storage, fp32 softmax and accumulation.
+ *
+ * Reference interface replaced (shihanqu/qwen3-embedding-webgpu-prepacked):
+ *   QKNormRopeKernel.createRun + encodeRun     src/webgpu/ops.ts:152-166, :15-19
+ *   CausalAttentionKernel.createRun + encode   src/webgpu/ops.ts:320-345
+ *   RoPE table build                           src/webgpu/model.ts:76-83
+ *
+ * Conventions
+ *   - All tensor pointers are device pointers owned by the caller; the
+ *     library never frees them. f16 tensors are passed as void*.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *     Launches are asynchronous on that stream.
+ *   - Every call returns a qwa_status; on failure qwa_last_error() gives
+ *     a message. No entry point aborts or exits the process.
+ *   - A qwa_ctx belongs to one device and is not thread-safe; use one
+ *     context per device (per host thread).
+ *   - cu_seqlens_host is a HOST array of batch+1 int32 offsets
+ *     (cu[0] = 0, non-decreasing). The context caches the device-side launch
+ *     plan per distinct (cu_seqlens, mode) and reuses it on later calls, so a
+ *     repeated shape costs no host->device traffic.
+ */
+#ifndef QWA_H
+#define QWA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QWA_API __attribute__((visibility("default")))
+#else
+#define QWA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum qwa_status {
+  QWA_OK = 0,
+  QWA_ERR_INVALID_ARG = 1,  /* bad pointer, shape, stride or alignment */
+  QWA_ERR_UNSUPPORTED = 2,  /* e.g. head counts other than 16/8, not sm_100 */
+  QWA_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed */
+  QWA_ERR_TIMEOUT = 4,      /* a device-side bounded wait gave up */
+  QWA_ERR_NO_DEVICE = 5
+} qwa_status;
+
+typedef enum qwa_mode {
+  QWA_MODE_AUTO = 0,   /* reference rule (ops.ts:328): sparse iff max_seqlen <= 8192 */
+  QWA_MODE_FULL = 1,   /* full causal */
+  QWA_MODE_SPARSE = 2  /* causal, keep k < prefix || k + window > q (ops.ts:220) */
+} qwa_mode;
+
+typedef struct qwa_ctx qwa_ctx;
+
+/* Create a context on CUDA device `device` (must be compute capability 10.x).
+ * Replaces the WebGPU device + pipeline construction of
+ * QKNormRopeKernel/CausalAttentionKernel constructors (ops.ts:153-156, :322-326). */
+QWA_API qwa_status qwa_create(int device, qwa_ctx **out);
+
+/* Release the context's device memory (plans, RoPE table, status word).
+ * Replaces Qwen3ExecutionPlan.destroy's release of AttentionRun.ownedBuffers
+ * (src/webgpu/model.ts:108-111). */
+QWA_API qwa_status qwa_destroy(qwa_ctx *ctx);
+
+/* Text of the last error on this context ("" if none). */
+QWA_API const char *qwa_last_error(const qwa_ctx *ctx);
+QWA_API const char *qwa_status_string(qwa_status status);
+
+/* Library version string. */
+QWA_API const char *qwa_version(void);
+
+/* Fused per-head RMSNorm + RoPE prologue over a packed ragged batch.
+ * Replaces QKNormRopeKernel.createRun + encodeRun (ops.ts:104-166).
+ *   qkv        f16 [total_tokens, qkv_stride]; q at column 0 (16x128),
+ *              k at column 2048 (8x128)  (inputStride of ops.ts:157)
+ *   q_weight, k_weight  f32 [128] each (attn_q_norm / attn_k_norm)
+ *   q_out      f16 [total_tokens, 16, 128]
+ *   k_out      f16 [total_tokens, 8, 128]
+ *   rope_table optional f32 [max_seqlen, 64, 2] (cos, sin) as built by
+ *              model.ts:76-83; NULL = the context's own table for `theta`.
+ * Position of a token = its index inside its request. */
+QWA_API qwa_status qwa_qk_norm_rope(qwa_ctx *ctx, const void *qkv, int64_t qkv_stride,
+                            const float *q_weight, const float *k_weight, void *q_out,
+                            void *k_out, const int32_t *cu_seqlens_host, int batch,
+                            float eps, float theta, const float *rope_table, void *stream);
+
+/* Padded-batch form with the reference's exact signature semantics
+ * (ops.ts:157): `tokens` rows, position = row % sequence. */
+QWA_API qwa_status qwa_qk_norm_rope_padded(qwa_ctx *ctx, const void *qkv, int64_t qkv_stride,
+                                   const float *q_weight, const float *k_weight, void *q_out,
+                                   void *k_out, int tokens, int sequence, float eps,
+                                   float theta, const float *rope_table, void *stream);
+
+/* Causal GQA prefill attention over a packed ragged batch (tcgen05 + TMA).
+ * Replaces CausalAttentionKernel.createRun + encode (ops.ts:168-345).
+ *   q    f16 [total_tokens, 16, 128]   (16-byte aligned)
+ *   k    f16 [total_tokens, 8, 128]
+ *   v    f16, head g of token t at v[t*v_stride + v_offset + g*128]
+ *        (valueStride/valueOffset of ops.ts:327; v+v_offset 16-byte aligned,
+ *        v_stride a multiple of 8)
+ *   out  f16 [total_tokens, 16, 128]
+ *   mode qwa_mode; prefix/window the sparse parameters (reference 176/432). */
+QWA_API qwa_status qwa_attention(qwa_ctx *ctx, const void *q, const void *k, const void *v,
+                         int64_t v_stride, int64_t v_offset, void *out,
+                         const int32_t *cu_seqlens_host, int batch, int mode, int prefix,
+                         int window, void *stream);
+
+/* Padded-batch form with the reference's createRun parameters (ops.ts:327):
+ * `batch` requests of exactly `sequence` rows each; q_heads/kv_heads must be
+ * 16/8. Mode AUTO as the reference (sparse iff sequence <= 8192). */
+QWA_API qwa_status qwa_attention_padded(qwa_ctx *ctx, const void *q, const void *k, const void *v,
+                                void *out, int batch, int sequence, int q_heads, int kv_heads,
+                                int64_t value_stride, int64_t value_offset, void *stream);
+
+/* Prologue + attention for one layer, in the order Qwen3ExecutionPlan encodes
+ * them (src/webgpu/model.ts:94-95,123). q_buf/k_buf receive the normed+roped
+ * q/k (caller-owned scratch, [T,16,128] / [T,8,128]); V is read from
+ * qkv[:, 3072:4096]. */
+QWA_API qwa_status qwa_prefill_attention_layer(qwa_ctx *ctx, const void *qkv, int64_t qkv_stride,
+                                       const float *q_weight, const float *k_weight,
+                                       void *q_buf, void *k_buf, void *out,
+                                       const int32_t *cu_seqlens_host, int batch, int mode,
+                                       int prefix, int window, float eps, float theta,
+                                       void *stream);
+
+/* Synchronise `stream` and report any device-side error recorded by the
+ * kernels since the last check (e.g. QWA_ERR_TIMEOUT from a bounded wait);
+ * clears the recorded error. */
+QWA_API qwa_status qwa_check(qwa_ctx *ctx, void *stream);
+
+/* Algorithmic work of an attention call: kept (q,k) pairs summed over the
+ * batch (per q-head; FLOPs = 8192 * pairs), and key tiles the kernel visits. */
+QWA_API qwa_status qwa_attention_work(const int32_t *cu_seqlens_host, int batch, int mode, int prefix,
+                              int window, int64_t *kept_pairs, int64_t *visited_tiles);
+
+/* Diagnostic: one 128x128x128 tensor-core tile through the same shared-memory
+ * descriptors the attention kernel uses. a [128,128] f16 (row-major, K
+ * contiguous), b [128,128] f16 (row-major, K contiguous), c f32 [128,128]
+ * = a @ b^T; then d f32 [128,128] = f16(c) @ vt, with the f16 copy of c
+ * taken from tensor memory and vt [128 k,128 n] f16 N-contiguous.
+ * No counterpart in the reference (it has no tensor-core path). */
+QWA_API qwa_status qwa_selftest_tile(qwa_ctx *ctx, const void *a, const void *b, const void *vt,
+                             float *c, float *d, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWA_H */

@@ -1,0 +1,271 @@
+/*
+ * CPU ORACLE -- test infrastructure only, never the product path.
+ *
+ * A plain-C restatement of the math of the reference's attention hot path
+ * (shihanqu/qwen3-embedding-webgpu-prepacked, WGSL shaders in
+ * src/webgpu/ops.ts), used by tests/, __graft_entry__.smoke() and the
+ * cpu_baseline / --impl reference legs of bench.py as the checker.
+ * Nothing in the shipped library links or calls this file.
+ *
+ * Parity status: UNPINNED against the reference itself. The reference has no
+ * CPU implementation of attention, RMSNorm or RoPE (its src/math holds only an
+ * f32->f16 converter) and its shaders run only under a browser WebGPU, which is
+ * unavailable on this box. What is pinned: the f32->f16 conversion
+ * (src/math/f16.ts:4-25) and halfToFloat known answers
+ * (tests/quantization.test.ts:5-9), plus analytic known-answer tests of
+ * the mask, RoPE and softmax semantics (tests/test_oracle.py).
+ *
+ * Numerics: inputs are the f16 values the kernels see; all arithmetic is
+ * fp64; results are returned unrounded (fp64) so a test can measure the
+ * device's error against the exact math.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* IEEE binary16 -> double. Follows halfToFloat semantics
+ * (src/gguf/quantization.ts; KATs tests/quantization.test.ts:5-9). */
+static double half_to_double(uint16_t h) {
+  int sign = (h >> 15) & 1;
+  int exponent = (h >> 10) & 0x1f;
+  int mantissa = h & 0x3ff;
+  double v;
+  if (exponent == 0) v = ldexp((double)mantissa, -24);
+  else if (exponent == 31) v = mantissa ? NAN : INFINITY;
+  else v = ldexp((double)(mantissa | 0x400), exponent - 25);
+  return sign ? -v : v;
+}
+
+double oracle_half_to_double(uint16_t h) { return half_to_double(h); }
+
+/* All 65536 f16 values as doubles, so the inner loops decode by lookup. */
+static double h2d_lut[65536];
+static int h2d_ready = 0;
+static void init_lut(void) {
+  if (h2d_ready) return;
+  for (int i = 0; i < 65536; ++i) h2d_lut[i] = half_to_double((uint16_t)i);
+  h2d_ready = 1;
+}
+#define H2D(x) h2d_lut[(x)]
+
+/* f32 -> f16 bits, round to nearest even; restates floatToHalf
+ * (src/math/f16.ts:4-25) bit for bit, including its subnormal path. */
+uint16_t oracle_float_to_half(float value) {
+  uint32_t bits;
+  memcpy(&bits, &value, 4);
+  uint32_t sign = (bits >> 16) & 0x8000u;
+  int exponent = (int)((bits >> 23) & 0xffu) - 127 + 15;
+  uint32_t mantissa = bits & 0x7fffffu;
+  if (exponent <= 0) {
+    if (exponent < -10) return (uint16_t)sign;
+    mantissa = (mantissa | 0x800000u) >> (1 - exponent);
+    return (uint16_t)(sign | ((mantissa + 0x1000u) >> 13));
+  }
+  if (exponent >= 31) return (uint16_t)(sign | 0x7c00u);
+  if (mantissa & 0x1000u) {
+    mantissa += 0x2000u;
+    if (mantissa & 0x800000u) {
+      mantissa = 0;
+      exponent += 1;
+      if (exponent >= 31) return (uint16_t)(sign | 0x7c00u);
+    }
+  }
+  return (uint16_t)(sign | ((uint32_t)exponent << 10) | (mantissa >> 13));
+}
+
+/* RoPE cos/sin table, src/webgpu/model.ts:76-83: angle = pos * theta^(-d/64)
+ * computed in double, stored as f32 pairs (cos, sin) at [(pos*64 + d)*2]. */
+void oracle_rope_table(double theta, int positions, float *table) {
+  for (int p = 0; p < positions; ++p)
+    for (int d = 0; d < 64; ++d) {
+      double angle = (double)p * pow(theta, -(double)d / 64.0);
+      table[(p * 64 + d) * 2] = (float)cos(angle);
+      table[(p * 64 + d) * 2 + 1] = (float)sin(angle);
+    }
+}
+
+/* Position of every packed token inside its request (cu_seqlens form). */
+static int position_of(const int32_t *cu, int batch, int64_t t) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) / 2;
+    if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return (int)(t - cu[lo]);
+}
+
+/* Fused per-head RMSNorm + RoPE, src/webgpu/ops.ts:104-150.
+ * For token t and each of 16 q-heads and 8 k-heads:
+ *   x = qkv[t*stride + (q ? 0 : 2048) + h*128 + d]
+ *   n = x / sqrt(sum(x^2)/128 + eps) * w[d]         (weights before RoPE)
+ *   out[d] = n[d]*cos + (d < 64 ? -n[d+64] : n[d-64]) * sin
+ * with (cos, sin) = table[pos*64 + d%64], pos = position inside the request
+ * (the reference's t % sequence for a padded batch).
+ * q_out: [T,16,128], k_out: [T,8,128], both fp64 unrounded. */
+void oracle_qk_norm_rope(const uint16_t *qkv, int64_t stride, const float *q_weight,
+                         const float *k_weight, const float *table, const int32_t *cu,
+                         int batch, double eps, double *q_out, double *k_out) {
+  int64_t tokens = cu[batch];
+#pragma omp parallel for schedule(static)
+  for (int64_t t = 0; t < tokens; ++t) {
+    int pos = position_of(cu, batch, t);
+    for (int ch = 0; ch < 24; ++ch) {
+      int is_q = ch < 16;
+      int h = is_q ? ch : ch - 16;
+      const uint16_t *src = qkv + t * stride + (is_q ? 0 : 2048) + h * 128;
+      const float *w = is_q ? q_weight : k_weight;
+      double x[128], n[128], sum = 0.0;
+      for (int d = 0; d < 128; ++d) { x[d] = half_to_double(src[d]); sum += x[d] * x[d]; }
+      double inv = 1.0 / sqrt(sum / 128.0 + eps);
+      for (int d = 0; d < 128; ++d) n[d] = x[d] * inv * (double)w[d];
+      double *dst = is_q ? q_out + (t * 16 + h) * 128 : k_out + (t * 8 + h) * 128;
+      for (int d = 0; d < 128; ++d) {
+        double c = table[(pos * 64 + d % 64) * 2], s = table[(pos * 64 + d % 64) * 2 + 1];
+        double rot = d < 64 ? -n[d + 64] : n[d - 64];
+        dst[d] = n[d] * c + rot * s;
+      }
+    }
+  }
+}
+
+/* Keep predicate of src/webgpu/ops.ts:220 for one request:
+ * keep key k for query q iff k <= q and, in sparse mode,
+ * (k < prefix || k + window > q). prefix/window are the reference's
+ * min(S,176) / min(S,432); using the unclipped constants gives the same
+ * kept set for every valid query (q < S). */
+int oracle_keep(int q, int k, int sparse, int prefix, int window) {
+  if (k > q) return 0;
+  if (!sparse) return 1;
+  return (k < prefix) || (k + window > q);
+}
+
+/* Mode rule of src/webgpu/ops.ts:328: the tiled kernel (sparse predicate)
+ * runs for sequence <= 8192, the chunked full-causal path above that.
+ * mode: 0 = AUTO (that rule on max_seqlen), 1 = FULL, 2 = SPARSE. */
+int oracle_resolve_sparse(int mode, int max_seqlen) {
+  if (mode == 1) return 0;
+  if (mode == 2) return 1;
+  return max_seqlen <= 8192;
+}
+
+/* Causal GQA attention, src/webgpu/ops.ts:168-241 (math only, fp64):
+ * out[t,h,:] = sum_k softmax_k(q.k / sqrt(128)) v_k over kept keys of the
+ * same request, kv head = h / 2. q: [T,16,128] f16, k: [T,8,128] f16,
+ * v: f16 at v[t*v_stride + v_offset + g*128 + d]. out: [T,16,128] fp64. */
+void oracle_attention(const uint16_t *q, const uint16_t *k, const uint16_t *v, int64_t v_stride,
+                      int64_t v_offset, const int32_t *cu, int batch, int mode, int prefix,
+                      int window, double *out) {
+  int max_len = 0;
+  for (int b = 0; b < batch; ++b) if (cu[b + 1] - cu[b] > max_len) max_len = cu[b + 1] - cu[b];
+  int sparse = oracle_resolve_sparse(mode, max_len);
+  int64_t tokens = cu[batch];
+  init_lut();
+  const double scale = 0.08838834764831845; /* 1/sqrt(128), ops.ts:224 */
+#pragma omp parallel
+  {
+    double *scores = (double *)malloc(sizeof(double) * (size_t)(max_len > 0 ? max_len : 1));
+    double acc[128], qv[128];
+#pragma omp for schedule(dynamic, 16)
+    for (int64_t idx = 0; idx < tokens * 16; ++idx) {
+      int64_t t = idx / 16;
+      int h = (int)(idx % 16), g = h / 2;
+      int b = 0;
+      while (cu[b + 1] <= t) ++b;
+      int64_t base = cu[b];
+      int qpos = (int)(t - base);
+      for (int d = 0; d < 128; ++d) qv[d] = H2D(q[(t * 16 + h) * 128 + d]);
+      double mx = -INFINITY;
+      for (int kp = 0; kp <= qpos; ++kp) {
+        if (!oracle_keep(qpos, kp, sparse, prefix, window)) { scores[kp] = -INFINITY; continue; }
+        const uint16_t *kr = k + ((base + kp) * 8 + g) * 128;
+        double s = 0.0;
+        for (int d = 0; d < 128; ++d) s += qv[d] * H2D(kr[d]);
+        s *= scale;
+        scores[kp] = s;
+        if (s > mx) mx = s;
+      }
+      double den = 0.0;
+      for (int d = 0; d < 128; ++d) acc[d] = 0.0;
+      for (int kp = 0; kp <= qpos; ++kp) {
+        if (scores[kp] == -INFINITY) continue;
+        double p = exp(scores[kp] - mx);
+        den += p;
+        const uint16_t *vr = v + (base + kp) * v_stride + v_offset + g * 128;
+        for (int d = 0; d < 128; ++d) acc[d] += p * H2D(vr[d]);
+      }
+      for (int d = 0; d < 128; ++d) out[(t * 16 + h) * 128 + d] = acc[d] / den;
+    }
+    free(scores);
+  }
+}
+
+/* Same math as oracle_attention for a sample of output rows only: rows[i]
+ * = t*16 + h; out_rows is [nrows,128] fp64. Lets tests check full-size
+ * workloads (e.g. 16x5000) against the oracle on a bounded sample. */
+void oracle_attention_rows(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                           int64_t v_stride, int64_t v_offset, const int32_t *cu, int batch,
+                           int mode, int prefix, int window, const int64_t *rows, int64_t nrows,
+                           double *out_rows) {
+  int max_len = 0;
+  for (int b = 0; b < batch; ++b) if (cu[b + 1] - cu[b] > max_len) max_len = cu[b + 1] - cu[b];
+  int sparse = oracle_resolve_sparse(mode, max_len);
+  const double scale = 0.08838834764831845;
+  init_lut();
+#pragma omp parallel
+  {
+    double *scores = (double *)malloc(sizeof(double) * (size_t)(max_len > 0 ? max_len : 1));
+    double acc[128], qv[128];
+#pragma omp for schedule(dynamic, 1)
+    for (int64_t i = 0; i < nrows; ++i) {
+      int64_t t = rows[i] / 16;
+      int h = (int)(rows[i] % 16), g = h / 2;
+      int b = 0;
+      while (cu[b + 1] <= t) ++b;
+      int64_t base = cu[b];
+      int qpos = (int)(t - base);
+      for (int d = 0; d < 128; ++d) qv[d] = H2D(q[(t * 16 + h) * 128 + d]);
+      double mx = -INFINITY;
+      for (int kp = 0; kp <= qpos; ++kp) {
+        if (!oracle_keep(qpos, kp, sparse, prefix, window)) { scores[kp] = -INFINITY; continue; }
+        const uint16_t *kr = k + ((base + kp) * 8 + g) * 128;
+        double s = 0.0;
+        for (int d = 0; d < 128; ++d) s += qv[d] * H2D(kr[d]);
+        scores[kp] = s * scale;
+        if (scores[kp] > mx) mx = scores[kp];
+      }
+      double den = 0.0;
+      for (int d = 0; d < 128; ++d) acc[d] = 0.0;
+      for (int kp = 0; kp <= qpos; ++kp) {
+        if (scores[kp] == -INFINITY) continue;
+        double p = exp(scores[kp] - mx);
+        den += p;
+        const uint16_t *vr = v + (base + kp) * v_stride + v_offset + g * 128;
+        for (int d = 0; d < 128; ++d) acc[d] += p * H2D(vr[d]);
+      }
+      for (int d = 0; d < 128; ++d) out_rows[i * 128 + d] = acc[d] / den;
+    }
+    free(scores);
+  }
+}
+
+/* Number of kept (q,k) pairs of one request of length len (for FLOP counts). */
+int64_t oracle_kept_pairs(int len, int sparse, int prefix, int window) {
+  int64_t n = 0;
+  for (int q = 0; q < len; ++q) {
+    if (!sparse) { n += q + 1; continue; }
+    for (int k = 0; k <= q; ++k) n += oracle_keep(q, k, sparse, prefix, window);
+  }
+  return n;
+}
+
+int oracle_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}

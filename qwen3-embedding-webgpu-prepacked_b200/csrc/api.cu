@@ -1,0 +1,496 @@
+// Host side of the C ABI declared in include/qwa.h.
+//
+// A context (qwa_ctx) owns, per device: the RoPE cos/sin table
+// (src/webgpu/model.ts:76-83, rebuilt when a longer sequence arrives), a
+// device status word that kernels write on a failed bounded wait, and a cache
+// of launch plans keyed by (cu_seqlens, resolved mode, prefix, window) -- the
+// counterpart of the reference engine's plan cache per "batch:sequence"
+// (src/webgpu/embedding-engine.ts:70-75). A plan holds the device copy of
+// cu_seqlens and the attention work list sorted longest-first.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/qwa.h"
+#include "internal.h"
+#include "ptx.cuh"
+
+using namespace qwa;
+
+namespace {
+
+constexpr int kSparseMaxSeq = 8192;  // src/webgpu/ops.ts:328
+constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128), ops.ts:224
+constexpr size_t kMaxPlans = 64;
+
+struct Plan {
+  int32_t* d_cu = nullptr;
+  AttnItem* d_items = nullptr;
+  int n_items = 0;
+  int batch = 0;
+  int total = 0;
+  int max_len = 0;
+  ~Plan() {
+    if (d_cu) cudaFree(d_cu);
+    if (d_items) cudaFree(d_items);
+  }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+}  // namespace
+
+struct qwa_ctx {
+  int device = 0;
+  std::string error;
+  int* d_status = nullptr;
+  float* d_rope = nullptr;
+  int rope_positions = 0;
+  float rope_theta = 0.f;
+  std::map<std::vector<int32_t>, std::unique_ptr<Plan>> plans;
+  std::vector<std::vector<int32_t>> plan_order;  // insertion order for eviction
+};
+
+namespace {
+
+qwa_status fail(qwa_ctx* ctx, qwa_status st, const char* fmt, ...) __attribute__((format(printf, 3, 4)));
+qwa_status fail(qwa_ctx* ctx, qwa_status st, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    ctx->error = buf;
+  }
+  return st;
+}
+
+#define QWA_CUDA(ctx, call)                                                                 \
+  do {                                                                                      \
+    cudaError_t e_ = (call);                                                                \
+    if (e_ != cudaSuccess)                                                                  \
+      return fail(ctx, QWA_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));       \
+  } while (0)
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+qwa_status ensure_encode(qwa_ctx* ctx) {
+  if (g_encode) return QWA_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return fail(ctx, QWA_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return QWA_OK;
+}
+
+// 3-D f16 map {128 dims, heads, rows}: head stride 256 B, row stride
+// row_stride_bytes; box {64, 1, 128} with 128-byte swizzle, so one load
+// lands as 128 rows x 128 B (the canonical SW128 K-major atom layout).
+qwa_status make_map(qwa_ctx* ctx, CUtensorMap* map, const void* base, int heads, int64_t rows,
+                    int64_t row_stride_bytes) {
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(row_stride_bytes)};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
+                        strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ctx, QWA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return QWA_OK;
+}
+
+qwa_status check_cu(qwa_ctx* ctx, const int32_t* cu, int batch, int* total, int* max_len) {
+  if (!cu) return fail(ctx, QWA_ERR_INVALID_ARG, "cu_seqlens_host is NULL");
+  if (batch < 1) return fail(ctx, QWA_ERR_INVALID_ARG, "batch must be >= 1 (got %d)", batch);
+  if (cu[0] != 0) return fail(ctx, QWA_ERR_INVALID_ARG, "cu_seqlens[0] must be 0");
+  int ml = 0;
+  for (int b = 0; b < batch; ++b) {
+    if (cu[b + 1] < cu[b])
+      return fail(ctx, QWA_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing (index %d)", b + 1);
+    ml = std::max(ml, cu[b + 1] - cu[b]);
+  }
+  *total = cu[batch];
+  *max_len = ml;
+  return QWA_OK;
+}
+
+int resolve_sparse(int mode, int max_len) {
+  if (mode == QWA_MODE_FULL) return 0;
+  if (mode == QWA_MODE_SPARSE) return 1;
+  return max_len <= kSparseMaxSeq ? 1 : 0;
+}
+
+// Plan lookup/creation. sparse < 0 requests a plan without attention items
+// (the prologue only needs the device cu_seqlens).
+qwa_status get_plan(qwa_ctx* ctx, const int32_t* cu, int batch, int sparse, int prefix,
+                    int window, cudaStream_t stream, Plan** out) {
+  std::vector<int32_t> key;
+  key.reserve(batch + 4);
+  key.push_back(sparse);
+  key.push_back(prefix);
+  key.push_back(window);
+  key.insert(key.end(), cu, cu + batch + 1);
+  auto it = ctx->plans.find(key);
+  if (it != ctx->plans.end()) {
+    *out = it->second.get();
+    return QWA_OK;
+  }
+  auto plan = std::make_unique<Plan>();
+  plan->batch = batch;
+  plan->total = cu[batch];
+  for (int b = 0; b < batch; ++b) plan->max_len = std::max(plan->max_len, cu[b + 1] - cu[b]);
+  QWA_CUDA(ctx, cudaMalloc(&plan->d_cu, sizeof(int32_t) * (batch + 1)));
+  QWA_CUDA(ctx, cudaMemcpyAsync(plan->d_cu, cu, sizeof(int32_t) * (batch + 1),
+                                cudaMemcpyHostToDevice, stream));
+  if (sparse >= 0) {
+    struct Work {
+      int tiles;
+      AttnItem item;
+    };
+    std::vector<Work> work;
+    for (int b = 0; b < batch; ++b) {
+      const int len = cu[b + 1] - cu[b];
+      for (int q0 = 0; q0 < len; q0 += kBlockM) {
+        const KeySchedule s = make_key_schedule(q0, len, sparse, prefix, window);
+        for (int g = 0; g < kKVHeads; ++g) work.push_back({s.n, make_int4(cu[b] + q0, q0, len, g)});
+      }
+    }
+    // Longest-first: the block scheduler dispatches in blockIdx order, which
+    // approximates LPT over the causal triangle.
+    std::stable_sort(work.begin(), work.end(),
+                     [](const Work& a, const Work& b) { return a.tiles > b.tiles; });
+    std::vector<AttnItem> items(work.size());
+    for (size_t i = 0; i < work.size(); ++i) items[i] = work[i].item;
+    plan->n_items = static_cast<int>(items.size());
+    if (!items.empty()) {
+      QWA_CUDA(ctx, cudaMalloc(&plan->d_items, sizeof(AttnItem) * items.size()));
+      QWA_CUDA(ctx, cudaMemcpyAsync(plan->d_items, items.data(), sizeof(AttnItem) * items.size(),
+                                    cudaMemcpyHostToDevice, stream));
+    }
+  }
+  if (ctx->plans.size() >= kMaxPlans) {
+    // Evict the oldest plan; cudaFree synchronises, so no launch still uses it.
+    ctx->plans.erase(ctx->plan_order.front());
+    ctx->plan_order.erase(ctx->plan_order.begin());
+  }
+  *out = plan.get();
+  ctx->plan_order.push_back(key);
+  ctx->plans.emplace(std::move(key), std::move(plan));
+  return QWA_OK;
+}
+
+// RoPE table of src/webgpu/model.ts:76-83: angle = pos * theta^(-d/64) in
+// double, stored as f32 (cos, sin) pairs.
+qwa_status ensure_rope(qwa_ctx* ctx, int positions, float theta, cudaStream_t stream) {
+  if (positions <= ctx->rope_positions && theta == ctx->rope_theta) return QWA_OK;
+  int n = std::max(positions, 1);
+  if (theta == ctx->rope_theta) n = std::max(n, 2 * ctx->rope_positions);
+  std::vector<float> host(static_cast<size_t>(n) * 128);
+  for (int p = 0; p < n; ++p)
+    for (int d = 0; d < 64; ++d) {
+      const double angle = static_cast<double>(p) * std::pow(static_cast<double>(theta), -d / 64.0);
+      host[(static_cast<size_t>(p) * 64 + d) * 2] = static_cast<float>(std::cos(angle));
+      host[(static_cast<size_t>(p) * 64 + d) * 2 + 1] = static_cast<float>(std::sin(angle));
+    }
+  if (ctx->d_rope) {
+    cudaFree(ctx->d_rope);
+    ctx->d_rope = nullptr;
+    ctx->rope_positions = 0;
+  }
+  QWA_CUDA(ctx, cudaMalloc(&ctx->d_rope, host.size() * sizeof(float)));
+  QWA_CUDA(ctx, cudaMemcpyAsync(ctx->d_rope, host.data(), host.size() * sizeof(float),
+                                cudaMemcpyHostToDevice, stream));
+  // The pageable copy above has been staged before return; keep ordering simple.
+  QWA_CUDA(ctx, cudaStreamSynchronize(stream));
+  ctx->rope_positions = n;
+  ctx->rope_theta = theta;
+  return QWA_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+qwa_status run_prologue(qwa_ctx* ctx, const void* qkv, int64_t qkv_stride, const float* q_weight,
+                        const float* k_weight, void* q_out, void* k_out, const int32_t* d_cu,
+                        int batch, int tokens, int padded_sequence, int positions, float eps,
+                        float theta, const float* rope_table, cudaStream_t stream) {
+  if (!qkv || !q_weight || !k_weight || !q_out || !k_out)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (qkv_stride < 3072 || qkv_stride % 8 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG,
+                "qkv_stride must be >= 3072 and a multiple of 8 (got %lld)",
+                static_cast<long long>(qkv_stride));
+  if (!aligned16(qkv) || !aligned16(q_weight) || !aligned16(k_weight) || !aligned16(q_out) ||
+      !aligned16(k_out) || (rope_table && !aligned16(rope_table)))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  if (!(eps >= 0.f)) return fail(ctx, QWA_ERR_INVALID_ARG, "eps must be >= 0");
+  const float* table = rope_table;
+  if (!table) {
+    qwa_status st = ensure_rope(ctx, positions, theta, stream);
+    if (st != QWA_OK) return st;
+    table = ctx->d_rope;
+  }
+  QWA_CUDA(ctx, launch_qk_norm_rope(static_cast<const __half*>(qkv), qkv_stride, q_weight,
+                                    k_weight, reinterpret_cast<const float2*>(table),
+                                    static_cast<__half*>(q_out), static_cast<__half*>(k_out), d_cu,
+                                    batch, tokens, padded_sequence, eps, stream));
+  return QWA_OK;
+}
+
+qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void* v,
+                         int64_t v_stride, int64_t v_offset, void* out, const int32_t* cu,
+                         int batch, int mode, int prefix, int window, cudaStream_t stream) {
+  int total = 0, max_len = 0;
+  qwa_status st = check_cu(ctx, cu, batch, &total, &max_len);
+  if (st != QWA_OK) return st;
+  if (mode < QWA_MODE_AUTO || mode > QWA_MODE_SPARSE)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "unknown mode %d", mode);
+  if (prefix < 0 || window < 1)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "prefix must be >= 0 and window >= 1");
+  if (total == 0) return QWA_OK;
+  if (!q || !k || !v || !out) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  const void* v_base = static_cast<const __half*>(v) + v_offset;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(out) || !aligned16(v_base))
+    return fail(ctx, QWA_ERR_INVALID_ARG,
+                "q, k, out and v + v_offset must be 16-byte aligned");
+  if (v_offset < 0 || v_stride % 8 != 0 || v_stride < v_offset + kKVHeads * kHeadDim)
+    return fail(ctx, QWA_ERR_INVALID_ARG,
+                "v_stride must be a multiple of 8 and >= v_offset + 1024");
+  st = ensure_encode(ctx);
+  if (st != QWA_OK) return st;
+  const int sparse = resolve_sparse(mode, max_len);
+  Plan* plan = nullptr;
+  st = get_plan(ctx, cu, batch, sparse, prefix, window, stream, &plan);
+  if (st != QWA_OK) return st;
+  CUtensorMap tm_q, tm_k, tm_v;
+  if ((st = make_map(ctx, &tm_q, q, kQHeads, total, kQHeads * kHeadDim * 2)) != QWA_OK) return st;
+  if ((st = make_map(ctx, &tm_k, k, kKVHeads, total, kKVHeads * kHeadDim * 2)) != QWA_OK) return st;
+  if ((st = make_map(ctx, &tm_v, v_base, kKVHeads, total, v_stride * 2)) != QWA_OK) return st;
+  AttnArgs args;
+  args.items = plan->d_items;
+  args.out = static_cast<__half*>(out);
+  args.sparse = sparse;
+  args.prefix = prefix;
+  args.window = window;
+  args.scale_log2 = kScale * 1.4426950408889634f;
+  args.status = ctx->d_status;
+  QWA_CUDA(ctx, launch_attention(tm_q, tm_k, tm_v, args, plan->n_items, stream));
+  return QWA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qwa_version(void) { return "qwa 0.1.0 (sm_100a tcgen05)"; }
+
+const char* qwa_status_string(qwa_status s) {
+  switch (s) {
+    case QWA_OK: return "ok";
+    case QWA_ERR_INVALID_ARG: return "invalid argument";
+    case QWA_ERR_UNSUPPORTED: return "unsupported";
+    case QWA_ERR_CUDA: return "CUDA error";
+    case QWA_ERR_TIMEOUT: return "device wait timed out";
+    case QWA_ERR_NO_DEVICE: return "no CUDA device";
+  }
+  return "unknown status";
+}
+
+const char* qwa_last_error(const qwa_ctx* ctx) { return ctx ? ctx->error.c_str() : ""; }
+
+qwa_status qwa_create(int device, qwa_ctx** out) {
+  if (!out) return QWA_ERR_INVALID_ARG;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return QWA_ERR_NO_DEVICE;
+  }
+  if (device < 0 || device >= count) return QWA_ERR_INVALID_ARG;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return QWA_ERR_CUDA;
+  if (prop.major != 10) return QWA_ERR_UNSUPPORTED;  // built for sm_100a only
+  DeviceGuard guard(device);
+  auto ctx = std::make_unique<qwa_ctx>();
+  ctx->device = device;
+  if (cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess) return QWA_ERR_CUDA;
+  if (cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess) return QWA_ERR_CUDA;
+  if (ensure_encode(ctx.get()) != QWA_OK) return QWA_ERR_CUDA;
+  *out = ctx.release();
+  return QWA_OK;
+}
+
+qwa_status qwa_destroy(qwa_ctx* ctx) {
+  if (!ctx) return QWA_OK;
+  {
+    DeviceGuard guard(ctx->device);
+    cudaDeviceSynchronize();
+    ctx->plans.clear();
+    if (ctx->d_rope) cudaFree(ctx->d_rope);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+  }
+  delete ctx;
+  return QWA_OK;
+}
+
+qwa_status qwa_check(qwa_ctx* ctx, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  QWA_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  int code = 0;
+  QWA_CUDA(ctx, cudaMemcpy(&code, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    QWA_CUDA(ctx, cudaMemset(ctx->d_status, 0, sizeof(int)));
+    return fail(ctx, QWA_ERR_TIMEOUT, "device-side bounded wait timed out (code 0x%x)", code);
+  }
+  return QWA_OK;
+}
+
+qwa_status qwa_qk_norm_rope(qwa_ctx* ctx, const void* qkv, int64_t qkv_stride,
+                            const float* q_weight, const float* k_weight, void* q_out,
+                            void* k_out, const int32_t* cu_seqlens_host, int batch, float eps,
+                            float theta, const float* rope_table, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int total = 0, max_len = 0;
+  qwa_status st = check_cu(ctx, cu_seqlens_host, batch, &total, &max_len);
+  if (st != QWA_OK) return st;
+  if (total == 0) return QWA_OK;
+  Plan* plan = nullptr;
+  st = get_plan(ctx, cu_seqlens_host, batch, -1, 0, 0, s, &plan);
+  if (st != QWA_OK) return st;
+  return run_prologue(ctx, qkv, qkv_stride, q_weight, k_weight, q_out, k_out, plan->d_cu, batch,
+                      total, 0, max_len, eps, theta, rope_table, s);
+}
+
+qwa_status qwa_qk_norm_rope_padded(qwa_ctx* ctx, const void* qkv, int64_t qkv_stride,
+                                   const float* q_weight, const float* k_weight, void* q_out,
+                                   void* k_out, int tokens, int sequence, float eps, float theta,
+                                   const float* rope_table, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  if (tokens < 0 || sequence < 1)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tokens must be >= 0 and sequence >= 1");
+  if (tokens == 0) return QWA_OK;
+  return run_prologue(ctx, qkv, qkv_stride, q_weight, k_weight, q_out, k_out, nullptr, 1, tokens,
+                      sequence, std::min(sequence, tokens), eps, theta, rope_table,
+                      static_cast<cudaStream_t>(stream));
+}
+
+qwa_status qwa_attention(qwa_ctx* ctx, const void* q, const void* k, const void* v,
+                         int64_t v_stride, int64_t v_offset, void* out,
+                         const int32_t* cu_seqlens_host, int batch, int mode, int prefix,
+                         int window, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  return run_attention(ctx, q, k, v, v_stride, v_offset, out, cu_seqlens_host, batch, mode, prefix,
+                       window, static_cast<cudaStream_t>(stream));
+}
+
+qwa_status qwa_attention_padded(qwa_ctx* ctx, const void* q, const void* k, const void* v,
+                                void* out, int batch, int sequence, int q_heads, int kv_heads,
+                                int64_t value_stride, int64_t value_offset, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  if (q_heads != kQHeads || kv_heads != kKVHeads)
+    return fail(ctx, QWA_ERR_UNSUPPORTED, "only 16 query heads / 8 kv heads are supported");
+  if (batch < 1 || sequence < 1)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "batch and sequence must be >= 1");
+  if (static_cast<int64_t>(batch) * sequence > 0x7fffffff)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "batch * sequence overflows int32");
+  std::vector<int32_t> cu(batch + 1);
+  for (int b = 0; b <= batch; ++b) cu[b] = b * sequence;
+  DeviceGuard guard(ctx->device);
+  return run_attention(ctx, q, k, v, value_stride, value_offset, out, cu.data(), batch,
+                       QWA_MODE_AUTO, 176, 432, static_cast<cudaStream_t>(stream));
+}
+
+qwa_status qwa_prefill_attention_layer(qwa_ctx* ctx, const void* qkv, int64_t qkv_stride,
+                                       const float* q_weight, const float* k_weight, void* q_buf,
+                                       void* k_buf, void* out, const int32_t* cu_seqlens_host,
+                                       int batch, int mode, int prefix, int window, float eps,
+                                       float theta, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  if (qkv_stride < 4096)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "qkv_stride must be >= 4096 (q, k and v columns)");
+  qwa_status st = qwa_qk_norm_rope(ctx, qkv, qkv_stride, q_weight, k_weight, q_buf, k_buf,
+                                   cu_seqlens_host, batch, eps, theta, nullptr, stream);
+  if (st != QWA_OK) return st;
+  DeviceGuard guard(ctx->device);
+  return run_attention(ctx, q_buf, k_buf, qkv, qkv_stride, 3072, out, cu_seqlens_host, batch, mode,
+                       prefix, window, static_cast<cudaStream_t>(stream));
+}
+
+qwa_status qwa_attention_work(const int32_t* cu, int batch, int mode, int prefix, int window,
+                              int64_t* kept_pairs, int64_t* visited_tiles) {
+  int total = 0, max_len = 0;
+  qwa_status st = check_cu(nullptr, cu, batch, &total, &max_len);
+  if (st != QWA_OK) return st;
+  if (prefix < 0 || window < 1) return QWA_ERR_INVALID_ARG;
+  const int sparse = resolve_sparse(mode, max_len);
+  int64_t pairs = 0, tiles = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int len = cu[b + 1] - cu[b];
+    for (int qi = 0; qi < len; ++qi) {
+      if (!sparse) {
+        pairs += qi + 1;
+      } else {
+        // keys [0, min(prefix, q+1)) plus (q - window, q] minus their overlap
+        const int64_t lo = std::max(0, qi - window + 1);
+        const int64_t pre = std::min(prefix, qi + 1);
+        const int64_t win = qi + 1 - lo;
+        const int64_t overlap = std::max<int64_t>(0, pre - lo);
+        pairs += pre + win - overlap;
+      }
+    }
+    for (int q0 = 0; q0 < len; q0 += kBlockM)
+      tiles += make_key_schedule(q0, len, sparse, prefix, window).n;
+  }
+  if (kept_pairs) *kept_pairs = pairs;
+  if (visited_tiles) *visited_tiles = tiles * kKVHeads;  // per kv group (two q heads each)
+  return QWA_OK;
+}
+
+qwa_status qwa_selftest_tile(qwa_ctx* ctx, const void* a, const void* b, const void* vt, float* c,
+                             float* d, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  if (!a || !b || !vt || !c || !d) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL pointer");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(vt))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "inputs must be 16-byte aligned");
+  DeviceGuard guard(ctx->device);
+  qwa_status st = ensure_encode(ctx);
+  if (st != QWA_OK) return st;
+  CUtensorMap ta, tb, tv;
+  if ((st = make_map(ctx, &ta, a, 1, 128, 256)) != QWA_OK) return st;
+  if ((st = make_map(ctx, &tb, b, 1, 128, 256)) != QWA_OK) return st;
+  if ((st = make_map(ctx, &tv, vt, 1, 128, 256)) != QWA_OK) return st;
+  QWA_CUDA(ctx, launch_selftest_tile(ta, tb, tv, c, d, ctx->d_status,
+                                     static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
+}  // extern "C"

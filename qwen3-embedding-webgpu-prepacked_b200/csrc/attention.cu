@@ -1,0 +1,501 @@
+// Causal / sparse GQA prefill attention for sm_100a (tcgen05 + TMA + TMEM).
+//
+// Replaces the reference's tiledFlashAttentionShader and the chunked two-pass
+// path (src/webgpu/ops.ts:168-316): same kept-pair predicate (ops.ts:220),
+// fp32 softmax/accumulation instead of the shader's f16 accumulators.
+//
+// One CTA = one 128-row query tile of one request for BOTH query heads
+// (2g, 2g+1) that share key/value head g, so each K/V tile is loaded once for
+// two MMA streams (GQA 2:1).
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer: Q tiles once, then K_j / V_j into a 4-slot ring
+//   warp 1      TMEM owner; lane 0 issues every tcgen05.mma and commit
+//   warps 2-5   softmax warpgroup A (head 2g):   one thread per query row
+//   warps 6-9   softmax warpgroup B (head 2g+1)
+//
+// TMEM (512 columns x 128 lanes, fp32):
+//   [0,128)   S_A = Q_A K_j^T   (P_A, f16 packed, overwrites columns [0,64))
+//   [128,256) S_B
+//   [256,384) O_A accumulator
+//   [384,512) O_B accumulator
+//
+// MMA issue order per key tile j (in-order tensor pipe):
+//   S_A(j), PV_B(j-1), S_B(j), PV_A(j)
+// so S_X(j)'s commit also proves PV_X(j-1) finished: the softmax warpgroup
+// can then rescale O_X in TMEM, and write P_X(j) over S_X(j), without a
+// separate correction warpgroup. Softmax of A overlaps the B MMAs and
+// vice versa.
+//
+// Masked key tiles are never visited: the key-tile schedule enumerates only
+// tiles that hold a kept pair (prefix tiles + window tiles in sparse mode);
+// elementwise masking runs only on tiles that straddle a mask boundary.
+#include <cuda_fp16.h>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace qwa {
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int kSlots = 4;
+constexpr uint32_t kTileBytes = kBlockN * kHeadDim * 2;  // 32 KB (two 16 KB swizzled halves)
+constexpr uint32_t kHalfBytes = kTileBytes / 2;
+constexpr uint32_t kQOff = 0;  // Q_A, Q_B
+constexpr uint32_t kSlotOff = 2 * kTileBytes;
+constexpr uint32_t kBarOff = kSlotOff + kSlots * kTileBytes;  // 196608
+enum Bar : int {
+  kQFull = 0,
+  kSlotFull = 1,                     // +slot
+  kSlotEmpty = kSlotFull + kSlots,   // +slot
+  kSFull = kSlotEmpty + kSlots,      // +X
+  kPFull = kSFull + 2,               // +X
+  kOFinal = kPFull + 2,
+  kNumBars = kOFinal + 1
+};
+constexpr uint32_t kHolderOff = kBarOff + 8 * kNumBars;
+constexpr uint32_t kAbortOff = kHolderOff + 4;
+constexpr uint32_t kSmemUsed = kAbortOff + 4;
+constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+constexpr uint32_t kIdescS = idesc_f16_f32(128, 128, false);   // Q K^T, both K-major
+constexpr uint32_t kIdescPV = idesc_f16_f32(128, 128, true);   // P V, V N-contiguous
+constexpr uint32_t kTmemCols = 512;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// S = Q K^T for a 128x128 tile, K = 128 in eight K=16 steps. Q and K tiles are
+// two 16 KB halves (dims 0-63, 64-127), each 128 rows x 128 B, 128B-swizzled.
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_smem, uint32_t k_smem) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+    mma_ss(d_tmem, smem_desc_sw128(q_smem + off, 16, 1024), smem_desc_sw128(k_smem + off, 16, 1024),
+           kIdescS, kk > 0 ? 1u : 0u);
+  }
+}
+
+// O (+)= P V: P (f16) from TMEM columns [p_tmem, p_tmem+64), V tile N-contiguous
+// (key rows of 128 B per 64-dim half): K=16 step = 16 key rows = 2048 B;
+// LBO = distance between dim halves, SBO = 8 key rows.
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
+                                         bool accumulate) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    mma_ts(d_tmem, p_tmem + kk * 8, smem_desc_sw128(v_smem + kk * 2048, kHalfBytes, 1024),
+           kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+__device__ __forceinline__ uint32_t low_bits(int n) {
+  return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : ((1u << n) - 1u));
+}
+
+// Scores of keys k0..k0+31 for query q: dropped pairs become -inf. The kept
+// set {k <= q, k < kcap, (k < prefix || k + window > q)} is built as a 32-bit
+// mask so the per-element cost is one bit test.
+__device__ __forceinline__ void mask_chunk(uint32_t (&a)[32], int k0, int q, int kcap, int sparse,
+                                           int prefix, int window) {
+  uint32_t m = low_bits(min(q, kcap - 1) - k0 + 1);
+  if (sparse) m &= low_bits(prefix - k0) | ~low_bits(q - window + 1 - k0);
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (!((m >> c) & 1u)) a[c] = __float_as_uint(-INFINITY);
+}
+
+__device__ __forceinline__ float chunk_max(const uint32_t (&a)[32]) {
+  float m0 = __uint_as_float(a[0]), m1 = __uint_as_float(a[1]);
+#pragma unroll
+  for (int c = 2; c < 32; c += 2) {
+    m0 = fmaxf(m0, __uint_as_float(a[c]));
+    m1 = fmaxf(m1, __uint_as_float(a[c + 1]));
+  }
+  return fmaxf(m0, m1);
+}
+
+// p = 2^(s*scale - m) for 32 raw scores; packs them as f16 pairs into a[0..15]
+// (in place, ascending, so every pair is read before its slot is reused) and
+// returns their fp32 sum.
+__device__ __forceinline__ float exp_pack_chunk(uint32_t (&a)[32], float scale, float m) {
+  float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float e0 = ex2(fmaf(__uint_as_float(a[2 * i]), scale, -m));
+    const float e1 = ex2(fmaf(__uint_as_float(a[2 * i + 1]), scale, -m));
+    sum0 += e0;
+    sum1 += e1;
+    a[i] = pack_half2(e0, e1);
+  }
+  return sum0 + sum1;
+}
+
+__device__ __forceinline__ bool tile_needs_mask(const KeySchedule& s, int j, int ks, int q0,
+                                                int q_last, int sparse, int prefix, int window) {
+  if (ks + kBlockN - 1 > q0) return true;                                   // causal edge
+  if (s.split && j < s.n_prefix && ks + kBlockN - 1 >= prefix) return true;  // prefix cut
+  if (sparse && ks + window <= q_last) return true;                         // window edge
+  return false;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_addr(smem);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kHolderOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
+  auto bar = [&](int i) -> uint32_t { return sbase + kBarOff + 8u * i; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const AttnItem item = args.items[blockIdx.x];
+  const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
+  const int base_row = row0 - q0;  // global row of the request's first token
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(kQFull), 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(bar(kSlotFull + s), 1);
+      mbar_init(bar(kSlotEmpty + s), 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bar(kSFull + x), 1);
+      mbar_init(bar(kPFull + x), 128);
+    }
+    mbar_init(bar(kOFinal), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(tmem_holder), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  const KeySchedule sch = make_key_schedule(q0, len, args.sparse, args.prefix, args.window);
+  const int n = sch.n;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(bar(kQFull), 2 * kTileBytes);
+      for (int x = 0; x < 2; ++x) {
+        const uint32_t dst = sbase + kQOff + x * kTileBytes;
+        tma_load_3d(dst, &tm_q, bar(kQFull), 0, 2 * g + x, row0);
+        tma_load_3d(dst + kHalfBytes, &tm_q, bar(kQFull), 64, 2 * g + x, row0);
+      }
+      for (int j = 0; j < n; ++j) {
+        const int krow = base_row + key_tile_start(sch, j);
+        for (int kv = 0; kv < 2; ++kv) {
+          const int c = 2 * j + kv;
+          const int s = c % kSlots;
+          const uint32_t ph = (c / kSlots) & 1;
+          if (!mbar_wait(bar(kSlotEmpty + s), ph ^ 1, abort_flag, args.status,
+                         kDevTimeoutSlotEmpty))
+            break;
+          const uint32_t dst = sbase + kSlotOff + s * kTileBytes;
+          const CUtensorMap* tm = kv == 0 ? &tm_k : &tm_v;
+          mbar_arrive_expect_tx(bar(kSlotFull + s), kTileBytes);
+          tma_load_3d(dst, tm, bar(kSlotFull + s), 0, g, krow);
+          tma_load_3d(dst + kHalfBytes, tm, bar(kSlotFull + s), 64, g, krow);
+        }
+        if (*abort_flag) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t t_s[2] = {tmem, tmem + 128};
+      const uint32_t t_o[2] = {tmem + 256, tmem + 384};
+      const uint32_t s_q[2] = {sbase + kQOff, sbase + kQOff + kTileBytes};
+      bool ok = mbar_wait(bar(kQFull), 0, abort_flag, args.status, kDevTimeoutQ);
+      int v_prev = 0;
+      for (int j = 0; ok && j < n; ++j) {
+        const int ck = 2 * j, sk = ck % kSlots;
+        const int cv = 2 * j + 1, sv = cv % kSlots;
+        const uint32_t k_smem = sbase + kSlotOff + sk * kTileBytes;
+        const uint32_t v_smem = sbase + kSlotOff + sv * kTileBytes;
+        if (!(ok = mbar_wait(bar(kSlotFull + sk), (ck / kSlots) & 1, abort_flag, args.status,
+                             kDevTimeoutSlotFull)))
+          break;
+        tc_fence_after();
+        issue_qk(t_s[0], s_q[0], k_smem);
+        tc_commit(bar(kSFull + 0));
+        if (j > 0) {
+          if (!(ok = mbar_wait(bar(kPFull + 1), (j - 1) & 1, abort_flag, args.status,
+                               kDevTimeoutPFull)))
+            break;
+          tc_fence_after();
+          issue_pv(t_o[1], t_s[1], sbase + kSlotOff + v_prev * kTileBytes, j - 1 > 0);
+          tc_commit(bar(kSlotEmpty + v_prev));
+        }
+        issue_qk(t_s[1], s_q[1], k_smem);
+        tc_commit(bar(kSFull + 1));
+        tc_commit(bar(kSlotEmpty + sk));
+        if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
+                             kDevTimeoutSlotFull)))
+          break;
+        if (!(ok = mbar_wait(bar(kPFull + 0), j & 1, abort_flag, args.status, kDevTimeoutPFull)))
+          break;
+        tc_fence_after();
+        issue_pv(t_o[0], t_s[0], v_smem, j > 0);
+        v_prev = sv;
+      }
+      if (ok && mbar_wait(bar(kPFull + 1), (n - 1) & 1, abort_flag, args.status,
+                          kDevTimeoutPFull)) {
+        tc_fence_after();
+        issue_pv(t_o[1], t_s[1], sbase + kSlotOff + v_prev * kTileBytes, n - 1 > 0);
+        tc_commit(bar(kSlotEmpty + v_prev));
+        tc_commit(bar(kOFinal));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int x = (warp - 2) >> 2;  // 0: head 2g, 1: head 2g+1
+    const int sub = warp & 3;       // TMEM lane sub-partition of this warp
+    const int row = sub * 32 + lane;
+    const int q = q0 + row;
+    const int q_last = (q0 + kBlockM < len ? q0 + kBlockM : len) - 1;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+    const uint32_t t_s = t_lane + x * 128;
+    const uint32_t t_o = t_lane + 256 + x * 128;
+    const float scale = args.scale_log2;
+    const int sparse = args.sparse, prefix = args.prefix, window = args.window;
+
+    float m_run = -INFINITY;  // running max of scaled scores (log2 domain)
+    float l_run = 0.f;        // running denominator relative to m_run
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!(ok = mbar_wait(bar(kSFull + x), j & 1, abort_flag, args.status, kDevTimeoutSFull)))
+        break;
+      tc_fence_after();
+      const int ks = key_tile_start(sch, j);
+      uint32_t a0[32], a1[32], a2[32], a3[32];
+      tmem_ld32(t_s + 0, a0);
+      tmem_ld32(t_s + 32, a1);
+      tmem_ld32(t_s + 64, a2);
+      tmem_ld32(t_s + 96, a3);
+      tmem_wait_ld();
+      reg_fence32(a0);
+      reg_fence32(a1);
+      reg_fence32(a2);
+      reg_fence32(a3);
+      if (tile_needs_mask(sch, j, ks, q0, q_last, sparse, prefix, window)) {
+        const int kcap = (sch.split && j < sch.n_prefix) ? prefix : 0x7fffffff;
+        mask_chunk(a0, ks + 0, q, kcap, sparse, prefix, window);
+        mask_chunk(a1, ks + 32, q, kcap, sparse, prefix, window);
+        mask_chunk(a2, ks + 64, q, kcap, sparse, prefix, window);
+        mask_chunk(a3, ks + 96, q, kcap, sparse, prefix, window);
+      }
+      // Raw scores; the softmax scale is folded into the exponent below.
+      const float tmax =
+          fmaxf(fmaxf(chunk_max(a0), chunk_max(a1)), fmaxf(chunk_max(a2), chunk_max(a3))) * scale;
+      const float m_new = fmaxf(m_run, tmax);
+      bool need = false;
+      float f = 1.f;
+      if (j == 0) {
+        m_run = m_new;
+      } else if (m_new > m_run + 8.f) {
+        // Lazy rescale: keep the stale max unless the new one exceeds it by
+        // more than 2^8 (P stays <= 256, exact enough in f16 and fp32).
+        need = true;
+        f = ex2(m_run - m_new);
+        l_run *= f;
+        m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      const float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use) +
+                        exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
+      l_run += sum;
+      tmem_st16(t_s + 0, a0);
+      tmem_st16(t_s + 16, a1);
+      tmem_st16(t_s + 32, a2);
+      tmem_st16(t_s + 48, a3);
+      if (__any_sync(0xffffffffu, need)) {
+        // O_X(j-1) is complete (S_X(j) was committed after PV_X(j-1)) and
+        // PV_X(j) waits for the arrival below.
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o + 32 * c, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st32(t_o + 32 * c, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(kPFull + x));
+    }
+    if (ok && mbar_wait(bar(kOFinal), 0, abort_flag, args.status, kDevTimeoutOFinal)) {
+      tc_fence_after();
+      const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+      const bool valid = q < len;
+      __half* dst = args.out + (static_cast<int64_t>(row0 + row) * kQHeads + 2 * g + x) * kHeadDim;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(t_o + 32 * c, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_half2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+            w.y = pack_half2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+            w.z = pack_half2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+            w.w = pack_half2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+            d4[v] = w;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- self test
+// One S tile and one PV tile through the same descriptors as the kernel above.
+__global__ void __launch_bounds__(128, 1)
+    selftest_tile_kernel(const __grid_constant__ CUtensorMap tm_a,
+                         const __grid_constant__ CUtensorMap tm_b,
+                         const __grid_constant__ CUtensorMap tm_v, float* c_out, float* d_out,
+                         int* status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t bar_ld = sbase + 3 * kTileBytes, bar_mma = bar_ld + 8;
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + 3 * kTileBytes + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + 3 * kTileBytes + 20);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(bar_ld, 1);
+    mbar_init(bar_mma, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_addr(holder), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *holder;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar_ld, 3 * kTileBytes);
+    const CUtensorMap* maps[3] = {&tm_a, &tm_b, &tm_v};
+    for (int i = 0; i < 3; ++i) {
+      tma_load_3d(sbase + i * kTileBytes, maps[i], bar_ld, 0, 0, 0);
+      tma_load_3d(sbase + i * kTileBytes + kHalfBytes, maps[i], bar_ld, 64, 0, 0);
+    }
+    if (mbar_wait(bar_ld, 0, abort_flag, status, kDevTimeoutSlotFull)) {
+      tc_fence_after();
+      issue_qk(tmem, sbase, sbase + kTileBytes);
+      tc_commit(bar_mma);
+    }
+  }
+  const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const int row = warp * 32 + lane;
+  bool ok = mbar_wait(bar_mma, 0, abort_flag, status, kDevTimeoutSFull);
+  if (ok) {
+    tc_fence_after();
+    uint32_t p[2][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld32(t_lane + 32 * c, r);
+      tmem_wait_ld();
+      reg_fence32(r);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) c_out[row * 128 + 32 * c + i] = __uint_as_float(r[i]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        p[c >> 1][(c & 1) * 16 + i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+    }
+    tmem_st32(t_lane, p[0]);
+    tmem_st32(t_lane + 32, p[1]);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (ok && threadIdx.x == 0) {
+    issue_pv(tmem + 128, tmem, sbase + 2 * kTileBytes, false);
+    tc_commit(bar_mma);
+  }
+  if (ok && mbar_wait(bar_mma, 1, abort_flag, status, kDevTimeoutOFinal)) {
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+      tmem_ld32(t_lane + 128 + 32 * c, r);
+      tmem_wait_ld();
+      reg_fence32(r);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) d_out[row * 128 + 32 * c + i] = __uint_as_float(r[i]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                             const CUtensorMap& tm_v, const AttnArgs& args, int num_items,
+                             cudaStream_t stream) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  if (num_items <= 0) return cudaSuccess;
+  attention_kernel<<<num_items, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_selftest_tile(const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+                                 const CUtensorMap& tm_v, float* c, float* d, int* status,
+                                 cudaStream_t stream) {
+  const uint32_t bytes = 3 * kTileBytes + 64 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(selftest_tile_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  selftest_tile_kernel<<<1, 128, bytes, stream>>>(tm_a, tm_b, tm_v, c, d, status);
+  return cudaGetLastError();
+}
+
+}  // namespace qwa

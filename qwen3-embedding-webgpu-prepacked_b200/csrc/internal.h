@@ -1,0 +1,80 @@
+// Internal declarations shared by the .cu files of libqwa (not part of the ABI).
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace qwa {
+
+constexpr int kQHeads = 16;
+constexpr int kKVHeads = 8;
+constexpr int kHeadDim = 128;
+constexpr int kBlockM = 128;  // query rows per tile
+constexpr int kBlockN = 128;  // keys per tile
+
+// One unit of attention work: a 128-row query tile of one request for the
+// two query heads (2g, 2g+1) that share key/value head g.
+//   x = global row of the tile's first query, y = its position in the request,
+//   z = request length, w = kv head g.
+using AttnItem = int4;
+
+// Key-tile schedule of one query tile. Shared by host (work counts, plan
+// ordering) and device (every warp role walks the same sequence).
+struct KeySchedule {
+  int n;         // key tiles visited
+  int n_prefix;  // leading tiles that only cover keys < prefix (split mode)
+  int ws;        // first key of the window tiles (split mode)
+  int split;     // 1: prefix tiles + window tiles; 0: contiguous from key 0
+};
+
+__host__ __device__ inline KeySchedule make_key_schedule(int q0, int len, int sparse, int prefix,
+                                                         int window) {
+  KeySchedule s;
+  const int q_last = (q0 + kBlockM < len ? q0 + kBlockM : len) - 1;
+  const int ws = q0 - (window - 1);  // first key any query of the tile keeps in its window
+  if (!sparse || ws <= prefix) {
+    s.split = 0;
+    s.n_prefix = 0;
+    s.ws = 0;
+    s.n = q_last / kBlockN + 1;
+  } else {
+    s.split = 1;
+    s.n_prefix = (prefix + kBlockN - 1) / kBlockN;
+    s.ws = ws;
+    s.n = s.n_prefix + (q_last - ws) / kBlockN + 1;
+  }
+  return s;
+}
+
+__host__ __device__ inline int key_tile_start(const KeySchedule& s, int j) {
+  return (!s.split || j < s.n_prefix) ? j * kBlockN : s.ws + (j - s.n_prefix) * kBlockN;
+}
+
+// Attention kernel arguments besides the three tensor maps.
+struct AttnArgs {
+  const AttnItem* items;
+  __half* out;  // [T, 16, 128]
+  int sparse;
+  int prefix;
+  int window;
+  float scale_log2;  // softmax scale * log2(e)
+  int* status;       // device status word (DeviceError codes)
+};
+
+cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                             const CUtensorMap& tm_v, const AttnArgs& args, int num_items,
+                             cudaStream_t stream);
+
+cudaError_t launch_selftest_tile(const CUtensorMap& tm_a, const CUtensorMap& tm_b,
+                                 const CUtensorMap& tm_v, float* c, float* d, int* status,
+                                 cudaStream_t stream);
+
+// Prologue. padded_sequence > 0: position = row % padded_sequence (the
+// reference's padded layout); otherwise positions come from cu_seqlens.
+cudaError_t launch_qk_norm_rope(const __half* qkv, int64_t qkv_stride, const float* q_weight,
+                                const float* k_weight, const float2* rope_table, __half* q_out,
+                                __half* k_out, const int32_t* cu_seqlens, int batch, int tokens,
+                                int padded_sequence, float eps, cudaStream_t stream);
+
+}  // namespace qwa

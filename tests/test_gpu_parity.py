@@ -1,0 +1,227 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the CPU oracle.
+
+Tolerance (the hot path's contract): per element max-abs <= 2e-3 and cosine
+>= 0.9999 per head output, against the oracle's exact (fp64) math on the same
+f16 inputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-3
+MIN_COS = 0.9999
+
+
+def _check(got: np.ndarray, ref: np.ndarray, what: str):
+    got = got.astype(np.float64)
+    err = np.abs(got - ref).max() if got.size else 0.0
+    assert np.isfinite(got).all(), f"{what}: non-finite output"
+    assert err <= MAX_ABS, f"{what}: max-abs {err:.3e}"
+    if got.ndim == 3 and got.size:  # [T, heads, 128]: cosine per head output
+        for h in range(got.shape[1]):
+            a, b = got[:, h].ravel(), ref[:, h].ravel()
+            cos = a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300)
+            assert cos >= MIN_COS, f"{what}: head {h} cosine {cos}"
+    return err
+
+
+def _dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def test_selftest_tile_matches_torch(pkg, cuda_dev):
+    g = torch.Generator(device="cpu").manual_seed(0)
+    a = torch.randn(128, 128, generator=g).half()
+    b = torch.randn(128, 128, generator=g).half()
+    vt = torch.randn(128, 128, generator=g).half()
+    c, d = pkg.attention.selftest_tile(a.cuda(), b.cuda(), vt.cuda())
+    c_ref = a.float() @ b.float().T
+    assert torch.allclose(c.cpu(), c_ref, atol=1e-3, rtol=1e-4), (c.cpu() - c_ref).abs().max()
+    d_ref = c_ref.half().float() @ vt.float()
+    assert torch.allclose(d.cpu(), d_ref, atol=2e-2, rtol=1e-3), (d.cpu() - d_ref).abs().max()
+
+
+@pytest.mark.parametrize("name", ["c1_single_50", "ragged_sparse_small"])
+def test_golden_fixture(pkg, cuda_dev, name):
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", name + ".npz"))
+    cu = [int(x) for x in g["cu_seqlens"]]
+    attn = pkg.attention
+    qkv = _dev(g["qkv"])
+    q, k = attn.qk_norm_rope(qkv, _dev(g["q_weight"]), _dev(g["k_weight"]), cu)
+    q16, k16 = g["q16"].astype(np.float64), g["k16"].astype(np.float64)
+    # within one f16 ulp of the exactly-rounded values
+    ulp_q = np.spacing(np.abs(g["q16"])).astype(np.float64)
+    ulp_k = np.spacing(np.abs(g["k16"])).astype(np.float64)
+    assert (np.abs(q.cpu().numpy() - q16) <= ulp_q).all()
+    assert (np.abs(k.cpu().numpy() - k16) <= ulp_k).all()
+    out = attn.attention(_dev(g["q16"]), _dev(g["k16"]), qkv, cu, 4096, 3072, int(g["mode"]),
+                         int(g["prefix"]), int(g["window"]))
+    attn.Context.for_device(0).check()
+    _check(out.cpu().numpy(), g["out"].astype(np.float64), name)
+
+
+def _random_case(lengths, seed):
+    rng = np.random.default_rng(seed)
+    cu = [0] + [int(x) for x in np.cumsum(lengths)]
+    qkv = rng.standard_normal((cu[-1], 4096), dtype=np.float32).astype(np.float16)
+    qw = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    return cu, qkv, qw, kw
+
+
+@pytest.mark.parametrize("lengths", [[50], [1, 2, 3], [130, 17, 500, 64], [5000]])
+def test_prologue_parity(pkg, oracle, cuda_dev, lengths):
+    cu, qkv, qw, kw = _random_case(lengths, 1)
+    q, k = pkg.attention.qk_norm_rope(_dev(qkv), _dev(qw), _dev(kw), cu)
+    q_ref, k_ref = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+    _check(q.cpu().numpy(), q_ref, "q")
+    _check(k.cpu().numpy(), k_ref, "k")
+
+
+def test_prologue_padded_matches_reference_positions(pkg, oracle, cuda_dev):
+    # QKNormRopeKernel.createRun semantics: position = row % sequence
+    B, S = 3, 40
+    cu, qkv, qw, kw = _random_case([S] * B, 2)
+    attn = pkg.attention
+    kern = attn.QKNormRopeKernel(0)
+    q = torch.empty(B * S, 16, 128, dtype=torch.float16, device="cuda")
+    k = torch.empty(B * S, 8, 128, dtype=torch.float16, device="cuda")
+    table = _dev(oracle.c_rope_table(1e6, S))
+    attn.encode_run(None, kern.create_run(_dev(qkv), _dev(qw), _dev(kw), q, k, B * S, S, 1e-6,
+                                          table, 4096))
+    q_ref, k_ref = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+    _check(q.cpu().numpy(), q_ref, "q")
+    _check(k.cpu().numpy(), k_ref, "k")
+
+
+ATTN_CASES = [
+    # (lengths, mode, prefix, window)
+    ([50], 0, 176, 432),
+    ([1], 0, 176, 432),
+    ([127, 128, 129], 0, 176, 432),
+    ([607, 608, 609], 0, 176, 432),
+    ([1500] * 4, 0, 176, 432),          # config 4 shape, sparse
+    ([500] * 16, 0, 176, 432),          # config 3 shape
+    ([1200, 0, 700], 1, 176, 432),      # full causal, empty request
+    ([600, 300], 2, 20, 40),            # split prefix/window tiles at short range
+    ([900], 2, 0, 64),                  # no prefix
+    ([1000], 2, 300, 50),               # prefix spanning 3 key tiles
+    ([700], 2, 176, 1),                 # window 1: prefix + diagonal only
+    ([2000], 1, 176, 432),
+]
+
+
+@pytest.mark.parametrize("lengths,mode,prefix,window", ATTN_CASES)
+def test_attention_parity(pkg, oracle, cuda_dev, lengths, mode, prefix, window):
+    rng = np.random.default_rng(sum(lengths) + mode)
+    cu = [0] + [int(x) for x in np.cumsum(lengths)]
+    T = cu[-1]
+    q = rng.standard_normal((T, 16, 128), dtype=np.float32).astype(np.float16)
+    k = rng.standard_normal((T, 8, 128), dtype=np.float32).astype(np.float16)
+    v = rng.standard_normal((T, 4096), dtype=np.float32).astype(np.float16)
+    out = pkg.attention.attention(_dev(q), _dev(k), _dev(v), cu, 4096, 3072, mode, prefix,
+                                  window)
+    pkg.attention.Context.for_device(0).check()
+    ref = oracle.c_attention(q, k, v, 4096, 3072, cu, mode, prefix, window)
+    _check(out.cpu().numpy(), ref, f"attention {lengths} mode {mode}")
+
+
+def test_ragged_layer_parity_config2(pkg, oracle, cuda_dev):
+    w = pkg.workloads.WORKLOADS["c2_ragged16"]
+    cu = w.cu_seqlens()
+    qkv, qw, kw = pkg.workloads.host_layer_inputs(w.tokens, seed=5)
+    attn = pkg.attention
+    T = w.tokens
+    q = torch.empty(T, 16, 128, dtype=torch.float16, device="cuda")
+    k = torch.empty(T, 8, 128, dtype=torch.float16, device="cuda")
+    out = attn.prefill_attention_layer(_dev(qkv), _dev(qw), _dev(kw), cu, q_buf=q, k_buf=k)
+    q_ref, k_ref = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+    _check(q.cpu().numpy(), q_ref, "q")
+    # end to end from qkv: oracle attention on the oracle's own f16 q/k
+    o_ref = oracle.c_attention(q_ref.astype(np.float16), k_ref.astype(np.float16), qkv, 4096, 3072,
+                               cu)
+    _check(out.cpu().numpy(), o_ref, "layer out")
+
+
+def test_padded_interface_matches_varlen(pkg, cuda_dev):
+    B, S = 3, 700
+    rng = np.random.default_rng(8)
+    q = _dev(rng.standard_normal((B * S, 16, 128), dtype=np.float32).astype(np.float16))
+    k = _dev(rng.standard_normal((B * S, 8, 128), dtype=np.float32).astype(np.float16))
+    v = _dev(rng.standard_normal((B * S, 1024), dtype=np.float32).astype(np.float16))
+    attn = pkg.attention
+    kern = attn.CausalAttentionKernel(0)
+    out_p = torch.empty_like(q)
+    kern.encode(None, kern.create_run(q, k, v, out_p, B, S))
+    out_v = attn.attention(q, k, v, [0, S, 2 * S, 3 * S], 1024, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(out_p, out_v)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_full_size_config5_sampled_rows(pkg, oracle, cuda_dev, mode):
+    """16 x 5000 (config 5): sampled output rows against the oracle, plus
+    size-independent properties on every row."""
+    lengths = [5000] * 16
+    cu = [0] + [int(x) for x in np.cumsum(lengths)]
+    T = cu[-1]
+    g = torch.Generator(device="cuda").manual_seed(123)
+    q = torch.randn(T, 16, 128, generator=g, device="cuda").half()
+    k = torch.randn(T, 8, 128, generator=g, device="cuda").half()
+    v = torch.randn(T, 1024, generator=g, device="cuda").half()
+    attn = pkg.attention
+    out = attn.attention(q, k, v, cu, 1024, 0, mode)
+    attn.Context.for_device(0).check()
+    rng = np.random.default_rng(mode)
+    toks = np.concatenate([rng.integers(0, T, 192), [0, 4999, 5000, 79999, 608, 609, 5607]])
+    rows = np.unique(toks[:, None] * 16 + rng.integers(0, 16, (len(toks), 2))).astype(np.int64)
+    ref = oracle.c_attention_rows(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), 1024, 0, cu,
+                                  rows, mode)
+    got = out.view(T * 16, 128)[torch.from_numpy(rows).cuda()].cpu().numpy().astype(np.float64)
+    err = np.abs(got - ref).max()
+    assert err <= MAX_ABS, err
+    # linearity in V and the constant-V property on every row
+    v2 = torch.randn(T, 1024, generator=g, device="cuda").half() * 0.5
+    out2 = attn.attention(q, k, v2, cu, 1024, 0, mode)
+    out12 = attn.attention(q, k, (v.float() + v2.float()).half(), cu, 1024, 0, mode)
+    lin = (out12.float() - out.float() - out2.float()).abs().max().item()
+    assert lin <= 4 * MAX_ABS, lin
+    const = torch.full((T, 1024), 0.75, dtype=torch.float16, device="cuda")
+    oc = attn.attention(q, k, const, cu, 1024, 0, mode)
+    assert (oc.float() - 0.75).abs().max().item() <= 1e-3
+
+
+def test_deterministic(pkg, cuda_dev):
+    rng = np.random.default_rng(4)
+    cu = [0, 900, 1000]
+    q = _dev(rng.standard_normal((1000, 16, 128), dtype=np.float32).astype(np.float16))
+    k = _dev(rng.standard_normal((1000, 8, 128), dtype=np.float32).astype(np.float16))
+    v = _dev(rng.standard_normal((1000, 1024), dtype=np.float32).astype(np.float16))
+    a = pkg.attention.attention(q, k, v, cu, 1024, 0)
+    b = pkg.attention.attention(q, k, v, cu, 1024, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_invalid_arguments_raise(pkg, cuda_dev):
+    attn = pkg.attention
+    q = torch.zeros(64, 16, 128, dtype=torch.float16, device="cuda")
+    k = torch.zeros(64, 8, 128, dtype=torch.float16, device="cuda")
+    v = torch.zeros(64, 1024, dtype=torch.float16, device="cuda")
+    v_big = torch.zeros(65, 1024, dtype=torch.float16, device="cuda")
+    with pytest.raises(attn._lib.QwaError) as e:  # v + v_offset not 16-byte aligned
+        attn.attention(q, k, v_big, [0, 64], 1024, 4)
+    assert e.value.status == attn._lib.QWA_ERR_INVALID_ARG
+    with pytest.raises(attn._lib.QwaError) as e:  # decreasing cu_seqlens
+        attn.attention(q, k, v, [0, 40, 30], 1024, 0)
+    assert e.value.status == attn._lib.QWA_ERR_INVALID_ARG
+    kern = attn.CausalAttentionKernel(0)
+    run = kern.create_run(q, k, v, torch.empty_like(q), 1, 64, q_heads=16, kv_heads=4)
+    with pytest.raises(attn._lib.QwaError) as e:
+        kern.encode(None, run)
+    assert e.value.status == attn._lib.QWA_ERR_UNSUPPORTED
+    with pytest.raises(ValueError):
+        attn.attention(q.float(), k, v, [0, 64])

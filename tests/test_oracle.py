@@ -1,0 +1,108 @@
+"""CPU oracle: pinned known answers and C-vs-numpy agreement (no GPU)."""
+import numpy as np
+import pytest
+
+
+def test_half_kats(oracle):
+    # tests/quantization.test.ts:5-9 of the reference (halfToFloat)
+    assert oracle.c_half_to_float(0x3C00) == 1.0
+    assert oracle.c_half_to_float(0xC000) == -2.0
+    assert oracle.c_half_to_float(0x0000) == 0.0
+
+
+def test_float_to_half_matches_numpy_rne(oracle):
+    # floatToHalf (src/math/f16.ts:4-25) is round-to-nearest-even like numpy
+    rng = np.random.default_rng(1)
+    vals = np.concatenate([rng.standard_normal(2000) * 10.0 ** rng.integers(-6, 5, 2000),
+                           [0.0, -0.0, 1.0, 65504.0, 65520.0, 1e-8, 6e-5, -3.14159]])
+    vals = vals.astype(np.float32)
+    ours = np.array([oracle.c_float_to_half(float(v)) for v in vals], dtype=np.uint16)
+    ref = vals.astype(np.float16).view(np.uint16)
+    assert np.array_equal(ours, ref)
+
+
+def test_rope_table_c_vs_numpy(oracle):
+    a = oracle.c_rope_table(1e6, 300)
+    b = oracle.np_rope_table(1e6, 300)
+    assert np.array_equal(a, b)
+    assert np.all(a[0, :, 0] == 1.0) and np.all(a[0, :, 1] == 0.0)
+
+
+def test_rope_position_zero_is_identity_and_rms_is_one(oracle):
+    rng = np.random.default_rng(3)
+    qkv = rng.standard_normal((1, 4096)).astype(np.float16)
+    ones = np.ones(128, np.float32)
+    q, k = oracle.c_qk_norm_rope(qkv, ones, ones, [0, 1])
+    x = qkv[0, :2048].astype(np.float64).reshape(16, 128)
+    n = x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6)
+    assert np.allclose(q[0], n, atol=1e-12)
+    assert np.allclose((q[0] ** 2).mean(-1), 1.0, atol=1e-5)
+
+
+@pytest.mark.parametrize("lengths", [[50], [3, 17, 40], [1, 129, 0, 64]])
+def test_prologue_c_vs_numpy(oracle, lengths):
+    rng = np.random.default_rng(len(lengths))
+    cu = [0] + list(np.cumsum(lengths))
+    qkv = rng.standard_normal((cu[-1], 4096)).astype(np.float16)
+    qw = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    q1, k1 = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+    q2, k2 = oracle.np_qk_norm_rope(qkv, qw, kw, cu)
+    assert np.abs(q1 - q2).max() < 1e-12 and np.abs(k1 - k2).max() < 1e-12
+
+
+@pytest.mark.parametrize("lengths,mode,prefix,window", [
+    ([50], 0, 176, 432), ([3, 17, 40], 1, 176, 432), ([200, 90], 2, 20, 40),
+    ([700], 0, 176, 432), ([1, 0, 33], 2, 5, 9)])
+def test_attention_c_vs_numpy(oracle, lengths, mode, prefix, window):
+    rng = np.random.default_rng(sum(lengths))
+    cu = [0] + list(np.cumsum(lengths))
+    T = cu[-1]
+    q = rng.standard_normal((T, 16, 128)).astype(np.float16)
+    k = rng.standard_normal((T, 8, 128)).astype(np.float16)
+    v = rng.standard_normal((T, 4096)).astype(np.float16)
+    a = oracle.c_attention(q, k, v, 4096, 3072, cu, mode, prefix, window)
+    b = oracle.np_attention(q, k, v, 4096, 3072, cu, mode, prefix, window)
+    assert np.abs(a - b).max() < 1e-10
+    rows = np.arange(0, T * 16, 7)
+    c = oracle.c_attention_rows(q, k, v, 4096, 3072, cu, rows, mode, prefix, window)
+    assert np.abs(c - a.reshape(T * 16, 128)[rows]).max() < 1e-12
+
+
+def test_attention_known_answers(oracle):
+    # identical keys -> uniform softmax -> mean of kept values
+    T = 700
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((T, 16, 128)).astype(np.float16)
+    k = np.tile(rng.standard_normal((1, 8, 128)).astype(np.float16), (T, 1, 1))
+    v = rng.standard_normal((T, 1024)).astype(np.float16)
+    out = oracle.c_attention(q, k, v, 1024, 0, [0, T], oracle.MODE_SPARSE)
+    vf = v.astype(np.float64)
+    for qpos in (0, 1, 175, 607, 608, 699):
+        m = oracle.keep_mask(T, True)[qpos]
+        expect = vf[m].reshape(-1, 8, 128).mean(0)
+        assert np.allclose(out[qpos, 0], expect[0], atol=1e-12)
+        assert np.allclose(out[qpos, 15], expect[7], atol=1e-12)
+    # query row 0 attends only to key 0
+    assert np.allclose(out[0].reshape(8, 2, 128)[:, 0], vf[0].reshape(8, 128), atol=1e-12)
+
+
+@pytest.mark.parametrize("S", [1, 15, 16, 17, 176, 431, 432, 433, 607, 608, 609, 1500, 5000])
+def test_mask_matches_wgsl_predicate_and_tile_skip(oracle, S):
+    m = oracle.keep_mask(S, oracle.resolve_sparse(oracle.MODE_AUTO, S))
+    qs = np.arange(S)
+    for qp in sorted(set([0, S // 2, S - 1] + list(qs[:: max(1, S // 40)]))):
+        lit = np.array([oracle.wgsl_keep(qp, kp, S) for kp in range(S)])
+        assert np.array_equal(lit, m[qp])
+    # the reference's 16-key block skip never drops a kept pair (ops.ts:209)
+    for qt in range(0, S, 16):
+        for kb in range(0, min(S, qt + 16), 16):
+            if oracle.wgsl_block_skipped(kb, qt, S):
+                assert not m[qt:qt + 16, kb:kb + 16].any()
+
+
+def test_kept_pairs_counts(oracle):
+    assert oracle.c_kept_pairs(500, True) == 500 * 501 // 2  # sparse is a no-op <= 608
+    assert oracle.c_kept_pairs(5000, False) == 5000 * 5001 // 2
+    assert 16 * oracle.c_kept_pairs(5000, True) == 45_687_552
+    assert oracle.resolve_sparse(oracle.MODE_AUTO, 8192) and not oracle.resolve_sparse(0, 8193)
