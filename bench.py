@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    # profiling aids: shrink the workload (never used for the reported line)
+    ap.add_argument("--requests", type=int, default=0, help="override request count")
+    ap.add_argument("--layers", type=int, default=0, help="override layer count")
     return ap.parse_args()
 
 
@@ -204,6 +207,12 @@ def main():
     attn = pkg.attention
     lib = pkg._lib.load()
     w = pkg.workloads.WORKLOADS[args.workload]
+    if args.requests or args.layers:
+        import dataclasses
+        w = dataclasses.replace(
+            w, name=w.name + "_reduced",
+            lengths=(w.lengths * 64)[:args.requests] if args.requests else w.lengths,
+            layers=args.layers or w.layers)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     ctx = attn.Context.for_device(local)

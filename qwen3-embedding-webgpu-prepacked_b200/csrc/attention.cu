@@ -72,25 +72,28 @@ __device__ __forceinline__ float ex2(float x) {
 
 // S = Q K^T for a 128x128 tile, K = 128 in eight K=16 steps. Q and K tiles are
 // two 16 KB halves (dims 0-63, 64-127), each 128 rows x 128 B, 128B-swizzled.
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_smem, uint32_t k_smem) {
+// q_desc/k_desc are the tiles' base descriptors (built once per CTA): a K step
+// only adds its byte offset >> 4 to the start-address field, so nothing but
+// the MMAs sits between consecutive issues. (Building a 64-bit descriptor
+// between tcgen05.mma issues halves the issue rate of a single thread:
+// measured 130 vs 64 cycles per 128x128x16 MMA on B200.)
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-    mma_ss(d_tmem, smem_desc_sw128(q_smem + off, 16, 1024), smem_desc_sw128(k_smem + off, 16, 1024),
-           kIdescS, kk > 0 ? 1u : 0u);
+    const uint64_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+    mma_ss(d_tmem, q_desc + off, k_desc + off, kIdescS, kk > 0 ? 1u : 0u);
   }
 }
 
 // O (+)= P V: P (f16) from TMEM columns [p_tmem, p_tmem+64), V tile N-contiguous
 // (key rows of 128 B per 64-dim half): K=16 step = 16 key rows = 2048 B;
-// LBO = distance between dim halves, SBO = 8 key rows.
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_smem,
+// LBO = distance between dim halves, SBO = 8 key rows (both in v_desc).
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint64_t v_desc,
                                          bool accumulate) {
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    mma_ts(d_tmem, p_tmem + kk * 8, smem_desc_sw128(v_smem + kk * 2048, kHalfBytes, 1024),
-           kIdescPV, (accumulate || kk > 0) ? 1u : 0u);
-  }
+  for (int kk = 0; kk < 8; ++kk)
+    mma_ts(d_tmem, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV,
+           (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ uint32_t low_bits(int n) {
@@ -109,14 +112,25 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&a)[32], int k0, int q, int
     if (!((m >> c) & 1u)) a[c] = __float_as_uint(-INFINITY);
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Row max of 32 raw scores: four independent chains of 3-input max (a single
+// dependent chain costs ~400 cycles per 128-column row).
 __device__ __forceinline__ float chunk_max(const uint32_t (&a)[32]) {
-  float m0 = __uint_as_float(a[0]), m1 = __uint_as_float(a[1]);
+  float m[4];
 #pragma unroll
-  for (int c = 2; c < 32; c += 2) {
-    m0 = fmaxf(m0, __uint_as_float(a[c]));
-    m1 = fmaxf(m1, __uint_as_float(a[c + 1]));
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t* p = a + 8 * c;
+    float v = fmax3(__uint_as_float(p[0]), __uint_as_float(p[1]), __uint_as_float(p[2]));
+    v = fmax3(v, __uint_as_float(p[3]), __uint_as_float(p[4]));
+    v = fmax3(v, __uint_as_float(p[5]), __uint_as_float(p[6]));
+    m[c] = fmaxf(v, __uint_as_float(p[7]));
   }
-  return fmaxf(m0, m1);
+  return fmax3(fmaxf(m[0], m[1]), m[2], m[3]);
 }
 
 // p = 2^(s*scale - m) for 32 raw scores; packs them as f16 pairs into a[0..15]
@@ -222,29 +236,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t t_s[2] = {tmem, tmem + 128};
       const uint32_t t_o[2] = {tmem + 256, tmem + 384};
-      const uint32_t s_q[2] = {sbase + kQOff, sbase + kQOff + kTileBytes};
+      const uint64_t q_desc0 = smem_desc_sw128(sbase + kQOff, 16, 1024);
+      const uint64_t q_desc1 = q_desc0 + (kTileBytes >> 4);
+      // slot s's descriptors = slot 0's + (s * kTileBytes) >> 4
+      const uint64_t k_desc0 = smem_desc_sw128(sbase + kSlotOff, 16, 1024);
+      const uint64_t v_desc0 = smem_desc_sw128(sbase + kSlotOff, kHalfBytes, 1024);
       bool ok = mbar_wait(bar(kQFull), 0, abort_flag, args.status, kDevTimeoutQ);
       int v_prev = 0;
       for (int j = 0; ok && j < n; ++j) {
         const int ck = 2 * j, sk = ck % kSlots;
         const int cv = 2 * j + 1, sv = cv % kSlots;
-        const uint32_t k_smem = sbase + kSlotOff + sk * kTileBytes;
-        const uint32_t v_smem = sbase + kSlotOff + sv * kTileBytes;
+        const uint64_t k_desc = k_desc0 + ((sk * kTileBytes) >> 4);
+        const uint64_t v_desc = v_desc0 + ((sv * kTileBytes) >> 4);
         if (!(ok = mbar_wait(bar(kSlotFull + sk), (ck / kSlots) & 1, abort_flag, args.status,
                              kDevTimeoutSlotFull)))
           break;
         tc_fence_after();
-        issue_qk(t_s[0], s_q[0], k_smem);
+        issue_qk(t_s[0], q_desc0, k_desc);
         tc_commit(bar(kSFull + 0));
         if (j > 0) {
           if (!(ok = mbar_wait(bar(kPFull + 1), (j - 1) & 1, abort_flag, args.status,
                                kDevTimeoutPFull)))
             break;
           tc_fence_after();
-          issue_pv(t_o[1], t_s[1], sbase + kSlotOff + v_prev * kTileBytes, j - 1 > 0);
+          issue_pv(t_o[1], t_s[1], v_desc0 + ((v_prev * kTileBytes) >> 4), j - 1 > 0);
           tc_commit(bar(kSlotEmpty + v_prev));
         }
-        issue_qk(t_s[1], s_q[1], k_smem);
+        issue_qk(t_s[1], q_desc1, k_desc);
         tc_commit(bar(kSFull + 1));
         tc_commit(bar(kSlotEmpty + sk));
         if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
@@ -253,13 +271,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(bar(kPFull + 0), j & 1, abort_flag, args.status, kDevTimeoutPFull)))
           break;
         tc_fence_after();
-        issue_pv(t_o[0], t_s[0], v_smem, j > 0);
+        issue_pv(t_o[0], t_s[0], v_desc, j > 0);
         v_prev = sv;
       }
       if (ok && mbar_wait(bar(kPFull + 1), (n - 1) & 1, abort_flag, args.status,
                           kDevTimeoutPFull)) {
         tc_fence_after();
-        issue_pv(t_o[1], t_s[1], sbase + kSlotOff + v_prev * kTileBytes, n - 1 > 0);
+        issue_pv(t_o[1], t_s[1], v_desc0 + ((v_prev * kTileBytes) >> 4), n - 1 > 0);
         tc_commit(bar(kSlotEmpty + v_prev));
         tc_commit(bar(kOFinal));
       }
@@ -417,7 +435,7 @@ __global__ void __launch_bounds__(128, 1)
     }
     if (mbar_wait(bar_ld, 0, abort_flag, status, kDevTimeoutSlotFull)) {
       tc_fence_after();
-      issue_qk(tmem, sbase, sbase + kTileBytes);
+      issue_qk(tmem, smem_desc_sw128(sbase, 16, 1024), smem_desc_sw128(sbase + kTileBytes, 16, 1024));
       tc_commit(bar_mma);
     }
   }
@@ -447,7 +465,7 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   if (ok && threadIdx.x == 0) {
-    issue_pv(tmem + 128, tmem, sbase + 2 * kTileBytes, false);
+    issue_pv(tmem + 128, tmem, smem_desc_sw128(sbase + 2 * kTileBytes, kHalfBytes, 1024), false);
     tc_commit(bar_mma);
   }
   if (ok && mbar_wait(bar_mma, 1, abort_flag, status, kDevTimeoutOFinal)) {
