@@ -149,6 +149,22 @@ QWA_API qwa_status qwa_attention_work(const int32_t *cu_seqlens_host, int batch,
 QWA_API qwa_status qwa_selftest_tile(qwa_ctx *ctx, const void *a, const void *b, const void *vt,
                              float *c, float *d, void *stream);
 
+/* Attention without any device allocation, for callers that cannot call
+ * cudaMalloc on their serving path (runtimes with a fixed, pre-planned memory
+ * arena; processes that hold no qwa_ctx). No counterpart in the reference.
+ * Same arguments and results as qwa_attention, on the current device, but the
+ * work list and status word live in a fixed 1 MiB device array owned by the
+ * library (held by every GPU that loads it until exit): a call needing more
+ * than 65,520 work items -- ceil(len/128) * 8 summed over requests, about one
+ * million tokens -- returns QWA_ERR_INVALID_ARG without launching. The first
+ * call on each device looks up that array's address; make it before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * race. Device-side timeouts are recorded in that array, not reported. */
+QWA_API qwa_status qwa_attention_noalloc(const void *q, const void *k, const void *v,
+                                         int64_t v_stride, int64_t v_offset, void *out,
+                                         const int32_t *cu_seqlens_host, int batch, int mode,
+                                         int prefix, int window, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,7 @@ SIGNATURES = {
     "qwa_check": (I32, [P, P]),
     "qwa_attention_work": (I32, [I32P, I32, I32, I32, I32, I64P, I64P]),
     "qwa_selftest_tile": (I32, [P, P, P, P, P, P, P]),
+    "qwa_attention_noalloc": (I32, [P, P, P, I64, I64, P, I32P, I32, I32, I32, I32, P]),
 }
 
 _lib = None
