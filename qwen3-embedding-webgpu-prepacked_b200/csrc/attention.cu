@@ -39,15 +39,17 @@ namespace qwa {
 namespace {
 
 constexpr int kThreads = 320;
-constexpr int kSlots = 4;
+constexpr int kSlots = 3;  // K/V ring (K_j and V_j alternate)
 constexpr uint32_t kTileBytes = kBlockN * kHeadDim * 2;  // 32 KB (two 16 KB swizzled halves)
 constexpr uint32_t kHalfBytes = kTileBytes / 2;
-constexpr uint32_t kQOff = 0;  // Q_A, Q_B
-constexpr uint32_t kSlotOff = 2 * kTileBytes;
-constexpr uint32_t kBarOff = kSlotOff + kSlots * kTileBytes;  // 196608
+constexpr uint32_t kQOff = 0;  // two Q buffers, each Q_A then Q_B
+constexpr uint32_t kQBufBytes = 2 * kTileBytes;
+constexpr uint32_t kSlotOff = 2 * kQBufBytes;
+constexpr uint32_t kBarOff = kSlotOff + kSlots * kTileBytes;  // 229376
 enum Bar : int {
-  kQFull = 0,
-  kSlotFull = 1,                     // +slot
+  kQFull = 0,                        // +Q buffer
+  kQEmpty = kQFull + 2,              // +Q buffer
+  kSlotFull = kQEmpty + 2,           // +slot
   kSlotEmpty = kSlotFull + kSlots,   // +slot
   kSFull = kSlotEmpty + kSlots,      // +X
   kPFull = kSFull + 2,               // +X
@@ -151,16 +153,20 @@ __device__ __forceinline__ float exp_pack_chunk(uint32_t (&a)[32], float scale, 
 
 __device__ __forceinline__ bool tile_needs_mask(const KeySchedule& s, int j, int ks, int q0,
                                                 int q_last, int sparse, int prefix, int window) {
-  if (ks + kBlockN - 1 > q0) return true;                                   // causal edge
-  if (s.split && j < s.n_prefix && ks + kBlockN - 1 >= prefix) return true;  // prefix cut
-  if (sparse && ks + window <= q_last) return true;                         // window edge
-  return false;
+  const int k_end = ks + kBlockN - 1;
+  if (k_end > q0) return true;  // causal edge
+  if (!sparse) return false;
+  if (s.split && j < s.n_prefix) return k_end >= prefix;  // prefix cut only
+  // window edge: some key of the tile at or above the prefix falls out of
+  // some query's window (keys below the prefix are always kept)
+  return k_end >= prefix && ks + window <= q_last;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args) {
+                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args,
+                     int num_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -171,12 +177,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const AttnItem item = args.items[blockIdx.x];
-  const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
-  const int base_row = row0 - q0;  // global row of the request's first token
+  const int sparse = args.sparse, prefix = args.prefix, window = args.window;
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(kQFull), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(kQFull + b), 1);
+      mbar_init(bar(kQEmpty + b), 1);
+    }
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(bar(kSlotFull + s), 1);
       mbar_init(bar(kSlotEmpty + s), 1);
@@ -201,84 +208,116 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  const KeySchedule sch = make_key_schedule(q0, len, args.sparse, args.prefix, args.window);
-  const int n = sch.n;
-
+  // Work items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ... (the
+  // list is sorted longest first). li counts this CTA's items, t its key
+  // tiles across items; every role walks the same sequence, so barrier
+  // phases follow from li and t.
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(bar(kQFull), 2 * kTileBytes);
-      for (int x = 0; x < 2; ++x) {
-        const uint32_t dst = sbase + kQOff + x * kTileBytes;
-        tma_load_3d(dst, &tm_q, bar(kQFull), 0, 2 * g + x, row0);
-        tma_load_3d(dst + kHalfBytes, &tm_q, bar(kQFull), 64, 2 * g + x, row0);
-      }
-      for (int j = 0; j < n; ++j) {
-        const int krow = base_row + key_tile_start(sch, j);
-        for (int kv = 0; kv < 2; ++kv) {
-          const int c = 2 * j + kv;
-          const int s = c % kSlots;
-          const uint32_t ph = (c / kSlots) & 1;
-          if (!mbar_wait(bar(kSlotEmpty + s), ph ^ 1, abort_flag, args.status,
-                         kDevTimeoutSlotEmpty))
-            break;
-          const uint32_t dst = sbase + kSlotOff + s * kTileBytes;
-          const CUtensorMap* tm = kv == 0 ? &tm_k : &tm_v;
-          mbar_arrive_expect_tx(bar(kSlotFull + s), kTileBytes);
-          tma_load_3d(dst, tm, bar(kSlotFull + s), 0, g, krow);
-          tma_load_3d(dst + kHalfBytes, tm, bar(kSlotFull + s), 64, g, krow);
+      int c = 0;  // K/V ring uses
+      bool ok = true;
+      for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
+        const AttnItem item = args.items[it];
+        const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
+        const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
+        const int qb = li & 1;
+        if (!(ok = mbar_wait(bar(kQEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, args.status,
+                             kDevTimeoutQ)))
+          break;
+        mbar_arrive_expect_tx(bar(kQFull + qb), kQBufBytes);
+        for (int x = 0; x < 2; ++x) {
+          const uint32_t dst = sbase + kQOff + qb * kQBufBytes + x * kTileBytes;
+          tma_load_3d(dst, &tm_q, bar(kQFull + qb), 0, 2 * g + x, row0);
+          tma_load_3d(dst + kHalfBytes, &tm_q, bar(kQFull + qb), 64, 2 * g + x, row0);
         }
-        if (*abort_flag) break;
+        for (int j = 0; ok && j < sch.n; ++j) {
+          const int krow = row0 - q0 + key_tile_start(sch, j);
+          for (int kv = 0; kv < 2; ++kv, ++c) {
+            const int s = c % kSlots;
+            if (!(ok = mbar_wait(bar(kSlotEmpty + s), ((c / kSlots) & 1) ^ 1, abort_flag,
+                                 args.status, kDevTimeoutSlotEmpty)))
+              break;
+            const uint32_t dst = sbase + kSlotOff + s * kTileBytes;
+            const CUtensorMap* tm = kv == 0 ? &tm_k : &tm_v;
+            mbar_arrive_expect_tx(bar(kSlotFull + s), kTileBytes);
+            tma_load_3d(dst, tm, bar(kSlotFull + s), 0, g, krow);
+            tma_load_3d(dst + kHalfBytes, tm, bar(kSlotFull + s), 64, g, krow);
+          }
+        }
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
+    // One flat stream over all key tiles of all items:
+    //   S_A(t), PV_B(t-1), S_B(t), PV_A(t)
+    // (the in-order tensor pipe then guarantees S_X(t+1) overwrites P_X(t)
+    // only after PV_X(t) read it). PV_B of an item's last tile is issued after
+    // the next item's S_A(0), so the next item's MMAs overlap this item's
+    // final softmax and epilogue.
     if (lane == 0) {
       const uint32_t t_s[2] = {tmem, tmem + 128};
       const uint32_t t_o[2] = {tmem + 256, tmem + 384};
       const uint64_t q_desc0 = smem_desc_sw128(sbase + kQOff, 16, 1024);
-      const uint64_t q_desc1 = q_desc0 + (kTileBytes >> 4);
       // slot s's descriptors = slot 0's + (s * kTileBytes) >> 4
       const uint64_t k_desc0 = smem_desc_sw128(sbase + kSlotOff, 16, 1024);
       const uint64_t v_desc0 = smem_desc_sw128(sbase + kSlotOff, kHalfBytes, 1024);
-      bool ok = mbar_wait(bar(kQFull), 0, abort_flag, args.status, kDevTimeoutQ);
-      int v_prev = 0;
-      for (int j = 0; ok && j < n; ++j) {
-        const int ck = 2 * j, sk = ck % kSlots;
-        const int cv = 2 * j + 1, sv = cv % kSlots;
-        const uint64_t k_desc = k_desc0 + ((sk * kTileBytes) >> 4);
-        const uint64_t v_desc = v_desc0 + ((sv * kTileBytes) >> 4);
-        if (!(ok = mbar_wait(bar(kSlotFull + sk), (ck / kSlots) & 1, abort_flag, args.status,
-                             kDevTimeoutSlotFull)))
+      bool ok = true;
+      int t = 0;
+      bool have_prev = false;  // PV_B of the previous tile still to issue
+      int prev_v = 0, prev_j = 0;
+      bool prev_last = false;
+      for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
+        const AttnItem item = args.items[it];
+        const KeySchedule sch = make_key_schedule(item.y, item.z, sparse, prefix, window);
+        const int qb = li & 1;
+        const uint64_t qa = q_desc0 + ((qb * kQBufBytes) >> 4);
+        const uint64_t qbd = qa + (kTileBytes >> 4);
+        if (!(ok = mbar_wait(bar(kQFull + qb), (li >> 1) & 1, abort_flag, args.status,
+                             kDevTimeoutQ)))
           break;
-        tc_fence_after();
-        issue_qk(t_s[0], q_desc0, k_desc);
-        tc_commit(bar(kSFull + 0));
-        if (j > 0) {
-          if (!(ok = mbar_wait(bar(kPFull + 1), (j - 1) & 1, abort_flag, args.status,
+        for (int j = 0; j < sch.n; ++j, ++t) {
+          const int ck = 2 * t, sk = ck % kSlots;
+          const int cv = 2 * t + 1, sv = cv % kSlots;
+          const uint64_t k_desc = k_desc0 + ((sk * kTileBytes) >> 4);
+          if (!(ok = mbar_wait(bar(kSlotFull + sk), (ck / kSlots) & 1, abort_flag, args.status,
+                               kDevTimeoutSlotFull)))
+            break;
+          tc_fence_after();
+          issue_qk(t_s[0], qa, k_desc);
+          tc_commit(bar(kSFull + 0));
+          if (have_prev) {
+            if (!(ok = mbar_wait(bar(kPFull + 1), (t - 1) & 1, abort_flag, args.status,
+                                 kDevTimeoutPFull)))
+              break;
+            tc_fence_after();
+            issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0);
+            tc_commit(bar(kSlotEmpty + prev_v));
+            if (prev_last) tc_commit(bar(kOFinal));
+          }
+          issue_qk(t_s[1], qbd, k_desc);
+          tc_commit(bar(kSFull + 1));
+          tc_commit(bar(kSlotEmpty + sk));
+          if (j == sch.n - 1) tc_commit(bar(kQEmpty + qb));
+          if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
+                               kDevTimeoutSlotFull)))
+            break;
+          if (!(ok = mbar_wait(bar(kPFull + 0), t & 1, abort_flag, args.status,
                                kDevTimeoutPFull)))
             break;
           tc_fence_after();
-          issue_pv(t_o[1], t_s[1], v_desc0 + ((v_prev * kTileBytes) >> 4), j - 1 > 0);
-          tc_commit(bar(kSlotEmpty + v_prev));
+          issue_pv(t_o[0], t_s[0], v_desc0 + ((sv * kTileBytes) >> 4), j > 0);
+          have_prev = true;
+          prev_v = sv;
+          prev_j = j;
+          prev_last = j == sch.n - 1;
         }
-        issue_qk(t_s[1], q_desc1, k_desc);
-        tc_commit(bar(kSFull + 1));
-        tc_commit(bar(kSlotEmpty + sk));
-        if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
-                             kDevTimeoutSlotFull)))
-          break;
-        if (!(ok = mbar_wait(bar(kPFull + 0), j & 1, abort_flag, args.status, kDevTimeoutPFull)))
-          break;
-        tc_fence_after();
-        issue_pv(t_o[0], t_s[0], v_desc, j > 0);
-        v_prev = sv;
       }
-      if (ok && mbar_wait(bar(kPFull + 1), (n - 1) & 1, abort_flag, args.status,
-                          kDevTimeoutPFull)) {
+      if (ok && have_prev &&
+          mbar_wait(bar(kPFull + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
         tc_fence_after();
-        issue_pv(t_o[1], t_s[1], v_desc0 + ((v_prev * kTileBytes) >> 4), n - 1 > 0);
-        tc_commit(bar(kSlotEmpty + v_prev));
+        issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0);
+        tc_commit(bar(kSlotEmpty + prev_v));
         tc_commit(bar(kOFinal));
       }
     }
@@ -287,82 +326,90 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int x = (warp - 2) >> 2;  // 0: head 2g, 1: head 2g+1
     const int sub = warp & 3;       // TMEM lane sub-partition of this warp
     const int row = sub * 32 + lane;
-    const int q = q0 + row;
-    const int q_last = (q0 + kBlockM < len ? q0 + kBlockM : len) - 1;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(sub * 32) << 16);
     const uint32_t t_s = t_lane + x * 128;
     const uint32_t t_o = t_lane + 256 + x * 128;
     const float scale = args.scale_log2;
-    const int sparse = args.sparse, prefix = args.prefix, window = args.window;
-
-    float m_run = -INFINITY;  // running max of scaled scores (log2 domain)
-    float l_run = 0.f;        // running denominator relative to m_run
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!(ok = mbar_wait(bar(kSFull + x), j & 1, abort_flag, args.status, kDevTimeoutSFull)))
-        break;
-      tc_fence_after();
-      const int ks = key_tile_start(sch, j);
-      uint32_t a0[32], a1[32], a2[32], a3[32];
-      tmem_ld32(t_s + 0, a0);
-      tmem_ld32(t_s + 32, a1);
-      tmem_ld32(t_s + 64, a2);
-      tmem_ld32(t_s + 96, a3);
-      tmem_wait_ld();
-      reg_fence32(a0);
-      reg_fence32(a1);
-      reg_fence32(a2);
-      reg_fence32(a3);
-      if (tile_needs_mask(sch, j, ks, q0, q_last, sparse, prefix, window)) {
-        const int kcap = (sch.split && j < sch.n_prefix) ? prefix : 0x7fffffff;
-        mask_chunk(a0, ks + 0, q, kcap, sparse, prefix, window);
-        mask_chunk(a1, ks + 32, q, kcap, sparse, prefix, window);
-        mask_chunk(a2, ks + 64, q, kcap, sparse, prefix, window);
-        mask_chunk(a3, ks + 96, q, kcap, sparse, prefix, window);
-      }
-      // Raw scores; the softmax scale is folded into the exponent below.
-      const float tmax =
-          fmaxf(fmaxf(chunk_max(a0), chunk_max(a1)), fmaxf(chunk_max(a2), chunk_max(a3))) * scale;
-      const float m_new = fmaxf(m_run, tmax);
-      bool need = false;
-      float f = 1.f;
-      if (j == 0) {
-        m_run = m_new;
-      } else if (m_new > m_run + 8.f) {
-        // Lazy rescale: keep the stale max unless the new one exceeds it by
-        // more than 2^8 (P stays <= 256, exact enough in f16 and fp32).
-        need = true;
-        f = ex2(m_run - m_new);
-        l_run *= f;
-        m_run = m_new;
-      }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      const float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use) +
-                        exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
-      l_run += sum;
-      tmem_st16(t_s + 0, a0);
-      tmem_st16(t_s + 16, a1);
-      tmem_st16(t_s + 32, a2);
-      tmem_st16(t_s + 48, a3);
-      if (__any_sync(0xffffffffu, need)) {
-        // O_X(j-1) is complete (S_X(j) was committed after PV_X(j-1)) and
-        // PV_X(j) waits for the arrival below.
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(t_o + 32 * c, o);
-          tmem_wait_ld();
-          reg_fence32(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st32(t_o + 32 * c, o);
+    int t = 0;
+    for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
+      const AttnItem item = args.items[it];
+      const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
+      const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
+      const int q = q0 + row;
+      const int q_last = (q0 + kBlockM < len ? q0 + kBlockM : len) - 1;
+      float m_run = -INFINITY;  // running max of scaled scores (log2 domain)
+      float l_run = 0.f;        // running denominator relative to m_run
+      for (int j = 0; j < sch.n; ++j, ++t) {
+        if (!(ok = mbar_wait(bar(kSFull + x), t & 1, abort_flag, args.status, kDevTimeoutSFull)))
+          break;
+        tc_fence_after();
+        const int ks = key_tile_start(sch, j);
+        uint32_t a0[32], a1[32], a2[32], a3[32];
+        tmem_ld32(t_s + 0, a0);
+        tmem_ld32(t_s + 32, a1);
+        tmem_ld32(t_s + 64, a2);
+        tmem_ld32(t_s + 96, a3);
+        tmem_wait_ld();
+        reg_fence32(a0);
+        reg_fence32(a1);
+        reg_fence32(a2);
+        reg_fence32(a3);
+        if (tile_needs_mask(sch, j, ks, q0, q_last, sparse, prefix, window)) {
+          const int kcap = (sch.split && j < sch.n_prefix) ? prefix : 0x7fffffff;
+          mask_chunk(a0, ks + 0, q, kcap, sparse, prefix, window);
+          mask_chunk(a1, ks + 32, q, kcap, sparse, prefix, window);
+          mask_chunk(a2, ks + 64, q, kcap, sparse, prefix, window);
+          mask_chunk(a3, ks + 96, q, kcap, sparse, prefix, window);
         }
+        // Raw scores; the softmax scale is folded into the exponent below.
+        const float tmax =
+            fmaxf(fmaxf(chunk_max(a0), chunk_max(a1)), fmaxf(chunk_max(a2), chunk_max(a3))) *
+            scale;
+        const float m_new = fmaxf(m_run, tmax);
+        bool need = false;
+        float f = 1.f;
+        if (j == 0) {
+          m_run = m_new;
+        } else if (m_new > m_run + 8.f) {
+          // Lazy rescale: keep the stale max unless the new one exceeds it by
+          // more than 2^8 (P stays <= 256, exact enough in f16 and fp32).
+          need = true;
+          f = ex2(m_run - m_new);
+          l_run *= f;
+          m_run = m_new;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        const float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use) +
+                          exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
+        l_run += sum;
+        tmem_st16(t_s + 0, a0);
+        tmem_st16(t_s + 16, a1);
+        tmem_st16(t_s + 32, a2);
+        tmem_st16(t_s + 48, a3);
+        if (__any_sync(0xffffffffu, need)) {
+          // O_X(j-1) is complete (S_X(j) was committed after PV_X(j-1)) and
+          // PV_X(j) waits for the arrival below.
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + 32 * c, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st32(t_o + 32 * c, o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(kPFull + x));
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(kPFull + x));
-    }
-    if (ok && mbar_wait(bar(kOFinal), 0, abort_flag, args.status, kDevTimeoutOFinal)) {
+      // Epilogue. O_X is read to registers (wait::ld) before this warpgroup's
+      // next P arrival, which is what the next item's first PV_X waits for.
+      if (!ok || !(ok = mbar_wait(bar(kOFinal), li & 1, abort_flag, args.status,
+                                  kDevTimeoutOFinal)))
+        break;
       tc_fence_after();
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool valid = q < len;
@@ -386,6 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      tc_fence_before();
     }
   }
 
@@ -501,7 +549,15 @@ cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
     configured = true;
   }
   if (num_items <= 0) return cudaSuccess;
-  attention_kernel<<<num_items, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, args);
+  static int sm_count = 0;
+  if (!sm_count) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+  }
+  const int grid = num_items < sm_count ? num_items : sm_count;  // persistent: one CTA per SM
+  attention_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, args, num_items);
   return cudaGetLastError();
 }
 
