@@ -232,14 +232,15 @@ def main():
     s = stream.cuda_stream
     P = attn._ptr
 
-    def layer_calls(qkv, qw, kw, ev=None):
+    def layer_calls(qkv, qw, kw, ev=None, out_buf=None):
+        o = out if out_buf is None else out_buf
         st = lib.qwa_qk_norm_rope(ctx.handle, P(qkv), 4096, P(qw), P(kw), P(q_buf), P(k_buf),
                                   cu_c, len(cu) - 1, 1e-6, 1e6, None, s)
         if st:
             pkg._lib.check(st, ctx.handle)
         if ev is not None:
             ev[0].record(stream)
-        st = lib.qwa_attention(ctx.handle, P(q_buf), P(k_buf), P(qkv), 4096, 3072, P(out), cu_c,
+        st = lib.qwa_attention(ctx.handle, P(q_buf), P(k_buf), P(qkv), 4096, 3072, P(o), cu_c,
                                len(cu) - 1, w.mode, 176, 432, s)
         if st:
             pkg._lib.check(st, ctx.handle)
@@ -293,28 +294,53 @@ def main():
     # crosses host->device from pinned memory, the layer output comes back
     e2e = None
     if not args.no_e2e:
+        # Pipelined over layers: H2D of layer l+1 and D2H of layer l-1 run on
+        # their own streams while layer l computes (double-buffered device
+        # inputs and outputs, ordered by events); PCIe is full duplex.
         host_in = [torch.empty(T, 4096, dtype=torch.float16).pin_memory() for _ in range(2)]
         for h in host_in:
             h.copy_(layers[0][0].cpu())
-        host_out = torch.empty(T, 16, 128, dtype=torch.float16).pin_memory()
-        dev_in = torch.empty(T, 4096, dtype=torch.float16, device=dev)
+        host_out = [torch.empty(T, 16, 128, dtype=torch.float16).pin_memory() for _ in range(2)]
+        dev_in = [torch.empty(T, 4096, dtype=torch.float16, device=dev) for _ in range(2)]
+        dev_out = [torch.empty(T, 16, 128, dtype=torch.float16, device=dev) for _ in range(2)]
+        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
         def e2e_step():
+            in_free = [None, None]   # compute done with dev_in[b]
+            out_free = [None, None]  # D2H done with dev_out[b]
             for l in range(L):
-                dev_in.copy_(host_in[l % 2], non_blocking=True)
-                layer_calls(dev_in, layers[l][1], layers[l][2])
-                host_out.copy_(out, non_blocking=True)
+                b = l % 2
+                with torch.cuda.stream(h2d):
+                    if in_free[b] is not None:
+                        h2d.wait_event(in_free[b])
+                    dev_in[b].copy_(host_in[b], non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(h2d)
+                stream.wait_event(ready)
+                if out_free[b] is not None:
+                    stream.wait_event(out_free[b])
+                layer_calls(dev_in[b], layers[l][1], layers[l][2], out_buf=dev_out[b])
+                done = torch.cuda.Event()
+                done.record(stream)
+                in_free[b] = done
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(done)
+                    host_out[b].copy_(dev_out[b], non_blocking=True)
+                    freed = torch.cuda.Event()
+                    freed.record(d2h)
+                    out_free[b] = freed
+            # the step ends when its last output is on the host
+            stream.wait_event(out_free[(L - 1) % 2])
 
-        with torch.cuda.stream(stream):
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
             e2e_step()
-            torch.cuda.synchronize()
-            barrier()
-            e0.record(stream)
-            for _ in range(args.e2e_steps):
-                e2e_step()
-            e1.record(stream)
-            torch.cuda.synchronize()
+        e1.record(stream)
+        torch.cuda.synchronize()
         barrier()
         e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
         if world > 1:
