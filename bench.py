@@ -134,6 +134,7 @@ def cpu_baseline(pkg, workload, seconds_budget=20.0):
     (prologue + attention over all its rows), scaled to tokens/s through 28
     layers."""
     from oracle import oracle
+    oracle.set_threads(os.cpu_count() or 1)  # torchrun sets OMP_NUM_THREADS=1
     L = int(max(workload.lengths))
     cu = [0, L]
     qkv, qw, kw = pkg.workloads.host_layer_inputs(L, seed=1)
@@ -161,6 +162,7 @@ def run_reference(args, world, rank):
         return
     pkg = importlib.import_module(PKG)
     from oracle import oracle
+    oracle.set_threads(os.cpu_count() or 1)  # all host threads (torchrun sets OMP_NUM_THREADS=1)
     w = pkg.workloads.WORKLOADS[args.workload]
     # a bounded sample per step: one request through one layer, all rows
     L = int(max(w.lengths))
@@ -201,6 +203,10 @@ def main():
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
         return
     import torch
     pkg = importlib.import_module(PKG)

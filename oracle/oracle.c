@@ -262,6 +262,15 @@ int64_t oracle_kept_pairs(int len, int sparse, int prefix, int window) {
   return n;
 }
 
+/* Use n OpenMP threads for the calls that follow (n <= 0: leave unchanged). */
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 int oracle_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

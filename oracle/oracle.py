@@ -71,6 +71,7 @@ def lib():
         L.oracle_kept_pairs.argtypes = [ctypes.c_int] * 4
         L.oracle_kept_pairs.restype = ctypes.c_int64
         L.oracle_threads.restype = ctypes.c_int
+        L.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = L
     return _lib
 
@@ -162,6 +163,11 @@ def c_attention_rows(q, k, v, v_stride: int, v_offset: int, cu_seqlens, rows,
 
 def c_kept_pairs(length: int, sparse: bool, prefix=PREFIX, window=WINDOW) -> int:
     return int(lib().oracle_kept_pairs(length, int(sparse), prefix, window))
+
+
+def set_threads(n: int) -> None:
+    """Number of OpenMP threads for later oracle calls."""
+    lib().oracle_set_threads(int(n))
 
 
 def threads() -> int:
