@@ -37,26 +37,33 @@ def _stale() -> bool:
                for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
+TRACE_LIB = os.path.join(HERE, "libqwa_trace.so")
+
+
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    """Build libqwa.so; trace=True builds the clock64-timeline variant
+    libqwa_trace.so (-DQWA_TRACE), used for kernel analysis only."""
+    lib = TRACE_LIB if trace else LIB
+    if not force and not trace and not _stale():
         return LIB
     objs = []
     for src in SOURCES:
-        obj = os.path.join(CSRC, src.replace(".cu", ".o"))
-        cmd = [nvcc(), *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
+        obj = os.path.join(CSRC, src.replace(".cu", ".trace.o" if trace else ".o"))
+        cmd = [nvcc(), *NVCC_FLAGS, *(["-DQWA_TRACE"] if trace else []), "-c",
+               os.path.join(CSRC, src), "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     subprocess.run([nvcc(), "-shared", *NVCC_FLAGS, *objs, "-o", tmp], check=True)
-    os.replace(tmp, LIB)
+    os.replace(tmp, lib)
     for o in objs:
         os.remove(o)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
-    print(LIB)
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv,
+                trace="--trace" in sys.argv))

@@ -58,6 +58,7 @@ struct qwa_ctx {
   float rope_theta = 0.f;
   std::map<std::vector<int32_t>, std::unique_ptr<Plan>> plans;
   std::vector<std::vector<int32_t>> plan_order;  // insertion order for eviction
+  unsigned long long* trace = nullptr;           // QWA_TRACE builds only
 };
 
 namespace {
@@ -298,6 +299,7 @@ qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void*
   args.window = window;
   args.scale_log2 = kScale * 1.4426950408889634f;
   args.status = ctx->d_status;
+  args.trace = ctx->trace;
   QWA_CUDA(ctx, launch_attention(tm_q, tm_k, tm_v, args, plan->n_items, stream));
   return QWA_OK;
 }
@@ -492,5 +494,16 @@ qwa_status qwa_selftest_tile(qwa_ctx* ctx, const void* a, const void* b, const v
                                      static_cast<cudaStream_t>(stream)));
   return QWA_OK;
 }
+
+#ifdef QWA_TRACE
+// Trace builds only (not part of include/qwa.h): attention launches record a
+// clock64 timeline of the first CTAs into `trace` (device buffer of
+// kTraceCtas * kTraceEvents * kTraceIters u64), or stop recording with NULL.
+QWA_API qwa_status qwa_debug_set_trace(qwa_ctx* ctx, unsigned long long* trace) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  ctx->trace = trace;
+  return QWA_OK;
+}
+#endif
 
 }  // extern "C"

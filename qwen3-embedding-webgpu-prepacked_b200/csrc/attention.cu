@@ -38,6 +38,25 @@
 namespace qwa {
 namespace {
 
+#ifdef QWA_TRACE
+// Trace events (clock64): producer K/V issue, MMA issue points, and for row 0
+// of each softmax warpgroup the S wait / TMEM load / max / exp / P arrive.
+enum TraceEvent : int {
+  kTrK = 0, kTrV, kTrMmaSA, kTrMmaPVB, kTrMmaSB, kTrMmaPVA,
+  kTrSmSReady, kTrSmLoaded = kTrSmSReady + 2, kTrSmMax = kTrSmLoaded + 2,
+  kTrSmExp = kTrSmMax + 2, kTrSmArrive = kTrSmExp + 2, kTrEpi = kTrSmArrive + 2
+};
+#define QWA_TR(ev, j)                                                                \
+  do {                                                                               \
+    if (args.trace && blockIdx.x < kTraceCtas && (j) < kTraceIters)                  \
+      args.trace[(blockIdx.x * kTraceEvents + (ev)) * kTraceIters + (j)] = clock64(); \
+  } while (0)
+#else
+#define QWA_TR(ev, j) \
+  do {                \
+  } while (0)
+#endif
+
 constexpr int kThreads = 320;
 constexpr int kSlots = 3;  // K/V ring (K_j and V_j alternate)
 constexpr uint32_t kTileBytes = kBlockN * kHeadDim * 2;  // 32 KB (two 16 KB swizzled halves)
@@ -241,6 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t dst = sbase + kSlotOff + s * kTileBytes;
             const CUtensorMap* tm = kv == 0 ? &tm_k : &tm_v;
             mbar_arrive_expect_tx(bar(kSlotFull + s), kTileBytes);
+            QWA_TR(kTrK + kv, c >> 1);
             tma_load_3d(dst, tm, bar(kSlotFull + s), 0, g, krow);
             tma_load_3d(dst + kHalfBytes, tm, bar(kSlotFull + s), 64, g, krow);
           }
@@ -284,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                kDevTimeoutSlotFull)))
             break;
           tc_fence_after();
+          QWA_TR(kTrMmaSA, t);
           issue_qk(t_s[0], qa, k_desc);
           tc_commit(bar(kSFull + 0));
           if (have_prev) {
@@ -291,10 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  kDevTimeoutPFull)))
               break;
             tc_fence_after();
+            QWA_TR(kTrMmaPVB, t - 1);
             issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0);
             tc_commit(bar(kSlotEmpty + prev_v));
             if (prev_last) tc_commit(bar(kOFinal));
           }
+          QWA_TR(kTrMmaSB, t);
           issue_qk(t_s[1], qbd, k_desc);
           tc_commit(bar(kSFull + 1));
           tc_commit(bar(kSlotEmpty + sk));
@@ -306,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                kDevTimeoutPFull)))
             break;
           tc_fence_after();
+          QWA_TR(kTrMmaPVA, t);
           issue_pv(t_o[0], t_s[0], v_desc0 + ((sv * kTileBytes) >> 4), j > 0);
           have_prev = true;
           prev_v = sv;
@@ -344,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(bar(kSFull + x), t & 1, abort_flag, args.status, kDevTimeoutSFull)))
           break;
         tc_fence_after();
+        if (row == 0) QWA_TR(kTrSmSReady + x, t);
         const int ks = key_tile_start(sch, j);
         uint32_t a0[32], a1[32], a2[32], a3[32];
         tmem_ld32(t_s + 0, a0);
@@ -355,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         reg_fence32(a1);
         reg_fence32(a2);
         reg_fence32(a3);
+        if (row == 0) QWA_TR(kTrSmLoaded + x, t);
         if (tile_needs_mask(sch, j, ks, q0, q_last, sparse, prefix, window)) {
           const int kcap = (sch.split && j < sch.n_prefix) ? prefix : 0x7fffffff;
           mask_chunk(a0, ks + 0, q, kcap, sparse, prefix, window);
@@ -379,10 +405,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           l_run *= f;
           m_run = m_new;
         }
+        if (row == 0) QWA_TR(kTrSmMax + x, t);
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
         const float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use) +
                           exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
         l_run += sum;
+        if (row == 0) QWA_TR(kTrSmExp + x, t);
         tmem_st16(t_s + 0, a0);
         tmem_st16(t_s + 16, a1);
         tmem_st16(t_s + 32, a2);
@@ -404,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar(kPFull + x));
+        if (row == 0) QWA_TR(kTrSmArrive + x, t);
       }
       // Epilogue. O_X is read to registers (wait::ld) before this warpgroup's
       // next P arrival, which is what the next item's first PV_X waits for.
@@ -411,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   kDevTimeoutOFinal)))
         break;
       tc_fence_after();
+      if (row == 0) QWA_TR(kTrEpi + x, t - 1);
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       const bool valid = q < len;
       __half* dst = args.out + (static_cast<int64_t>(row0 + row) * kQHeads + 2 * g + x) * kHeadDim;

@@ -60,7 +60,15 @@ struct AttnArgs {
   int window;
   float scale_log2;  // softmax scale * log2(e)
   int* status;       // device status word (DeviceError codes)
+  unsigned long long* trace;  // QWA_TRACE builds only: per-role clock64 timeline
 };
+
+// Timeline layout of a QWA_TRACE build: trace[(cta * kTraceEvents + event) *
+// kTraceIters + key_tile] = clock64() for the first kTraceCtas CTAs (key_tile
+// counts the CTA's tiles across its work items).
+constexpr int kTraceCtas = 4;
+constexpr int kTraceEvents = 20;
+constexpr int kTraceIters = 256;
 
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const AttnArgs& args, int num_items,

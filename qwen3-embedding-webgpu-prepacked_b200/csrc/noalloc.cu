@@ -151,6 +151,7 @@ extern "C" qwa_status qwa_attention_noalloc(const void* q, const void* k, const 
   args.window = window;
   args.scale_log2 = 0.08838834764831845f * 1.4426950408889634f;
   args.status = status;
+  args.trace = nullptr;
   if (launch_attention(tm_q, tm_k, tm_v, args, static_cast<int>(items.size()), s) != cudaSuccess)
     return QWA_ERR_CUDA;
   return QWA_OK;
