@@ -98,23 +98,26 @@ __device__ __forceinline__ float ex2(float x) {
 // the MMAs sits between consecutive issues. (Building a 64-bit descriptor
 // between tcgen05.mma issues halves the issue rate of a single thread:
 // measured 130 vs 64 cycles per 128x128x16 MMA on B200.)
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc) {
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint64_t q_desc, uint64_t k_desc,
+                                         uint32_t idesc = kIdescS) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk) {
     const uint64_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
-    mma_ss(d_tmem, q_desc + off, k_desc + off, kIdescS, kk > 0 ? 1u : 0u);
+    mma_ss(d_tmem, q_desc + off, k_desc + off, idesc, kk > 0 ? 1u : 0u);
   }
 }
 
 // O (+)= P V: P (f16) from TMEM columns [p_tmem, p_tmem+64), V tile N-contiguous
 // (key rows of 128 B per 64-dim half): K=16 step = 16 key rows = 2048 B;
 // LBO = distance between dim halves, SBO = 8 key rows (both in v_desc).
+// nk = key steps of 16 actually used (tile width / 16).
 __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint64_t v_desc,
-                                         bool accumulate) {
+                                         bool accumulate, int nk = 8) {
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    mma_ts(d_tmem, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV,
-           (accumulate || kk > 0) ? 1u : 0u);
+    if (kk < nk)
+      mma_ts(d_tmem, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV,
+             (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ uint32_t low_bits(int n) {
@@ -285,11 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int t = 0;
       bool have_prev = false;  // PV_B of the previous tile still to issue
-      int prev_v = 0, prev_j = 0;
+      int prev_v = 0, prev_j = 0, prev_nk = 8;
       bool prev_last = false;
       for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
         const AttnItem item = args.items[it];
         const KeySchedule sch = make_key_schedule(item.y, item.z, sparse, prefix, window);
+        const int q_last = (item.y + kBlockM < item.z ? item.y + kBlockM : item.z) - 1;
         const int qb = li & 1;
         const uint64_t qa = q_desc0 + ((qb * kQBufBytes) >> 4);
         const uint64_t qbd = qa + (kTileBytes >> 4);
@@ -305,7 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           tc_fence_after();
           QWA_TR(kTrMmaSA, t);
-          issue_qk(t_s[0], qa, k_desc);
+          const int width = key_tile_width(sch, j, q_last, prefix);
+          const uint32_t idesc = idesc_f16_f32(128, width, false);
+          issue_qk(t_s[0], qa, k_desc, idesc);
           tc_commit(bar(kSFull + 0));
           if (have_prev) {
             if (!(ok = mbar_wait(bar(kPFull + 1), (t - 1) & 1, abort_flag, args.status,
@@ -313,12 +319,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             tc_fence_after();
             QWA_TR(kTrMmaPVB, t - 1);
-            issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0);
+            issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0, prev_nk);
             tc_commit(bar(kSlotEmpty + prev_v));
             if (prev_last) tc_commit(bar(kOFinal));
           }
           QWA_TR(kTrMmaSB, t);
-          issue_qk(t_s[1], qbd, k_desc);
+          issue_qk(t_s[1], qbd, k_desc, idesc);
           tc_commit(bar(kSFull + 1));
           tc_commit(bar(kSlotEmpty + sk));
           if (j == sch.n - 1) tc_commit(bar(kQEmpty + qb));
@@ -330,17 +336,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           tc_fence_after();
           QWA_TR(kTrMmaPVA, t);
-          issue_pv(t_o[0], t_s[0], v_desc0 + ((sv * kTileBytes) >> 4), j > 0);
+          issue_pv(t_o[0], t_s[0], v_desc0 + ((sv * kTileBytes) >> 4), j > 0, width / 16);
           have_prev = true;
           prev_v = sv;
           prev_j = j;
+          prev_nk = width / 16;
           prev_last = j == sch.n - 1;
         }
       }
       if (ok && have_prev &&
           mbar_wait(bar(kPFull + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
         tc_fence_after();
-        issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0);
+        issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0, prev_nk);
         tc_commit(bar(kSlotEmpty + prev_v));
         tc_commit(bar(kOFinal));
       }
@@ -370,28 +377,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (row == 0) QWA_TR(kTrSmSReady + x, t);
         const int ks = key_tile_start(sch, j);
+        // narrow tile (width <= 64): only its first two 32-column chunks exist;
+        // columns past the width are stale TMEM and always masked below
+        const bool narrow = key_tile_width(sch, j, q_last, prefix) <= 64;
         uint32_t a0[32], a1[32], a2[32], a3[32];
         tmem_ld32(t_s + 0, a0);
         tmem_ld32(t_s + 32, a1);
-        tmem_ld32(t_s + 64, a2);
-        tmem_ld32(t_s + 96, a3);
+        if (!narrow) {
+          tmem_ld32(t_s + 64, a2);
+          tmem_ld32(t_s + 96, a3);
+        }
         tmem_wait_ld();
         reg_fence32(a0);
         reg_fence32(a1);
-        reg_fence32(a2);
-        reg_fence32(a3);
+        if (!narrow) {
+          reg_fence32(a2);
+          reg_fence32(a3);
+        }
         if (row == 0) QWA_TR(kTrSmLoaded + x, t);
         if (tile_needs_mask(sch, j, ks, q0, q_last, sparse, prefix, window)) {
           const int kcap = (sch.split && j < sch.n_prefix) ? prefix : 0x7fffffff;
           mask_chunk(a0, ks + 0, q, kcap, sparse, prefix, window);
           mask_chunk(a1, ks + 32, q, kcap, sparse, prefix, window);
-          mask_chunk(a2, ks + 64, q, kcap, sparse, prefix, window);
-          mask_chunk(a3, ks + 96, q, kcap, sparse, prefix, window);
+          if (!narrow) {
+            mask_chunk(a2, ks + 64, q, kcap, sparse, prefix, window);
+            mask_chunk(a3, ks + 96, q, kcap, sparse, prefix, window);
+          }
         }
         // Raw scores; the softmax scale is folded into the exponent below.
-        const float tmax =
-            fmaxf(fmaxf(chunk_max(a0), chunk_max(a1)), fmaxf(chunk_max(a2), chunk_max(a3))) *
-            scale;
+        float tmax = fmaxf(chunk_max(a0), chunk_max(a1));
+        if (!narrow) tmax = fmaxf(tmax, fmaxf(chunk_max(a2), chunk_max(a3)));
+        tmax *= scale;
         const float m_new = fmaxf(m_run, tmax);
         bool need = false;
         float f = 1.f;
@@ -407,14 +423,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (row == 0) QWA_TR(kTrSmMax + x, t);
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        const float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use) +
-                          exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
+        float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use);
+        if (!narrow) sum += exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
         l_run += sum;
         if (row == 0) QWA_TR(kTrSmExp + x, t);
         tmem_st16(t_s + 0, a0);
         tmem_st16(t_s + 16, a1);
-        tmem_st16(t_s + 32, a2);
-        tmem_st16(t_s + 48, a3);
+        if (!narrow) {
+          tmem_st16(t_s + 32, a2);
+          tmem_st16(t_s + 48, a3);
+        }
         if (__any_sync(0xffffffffu, need)) {
           // O_X(j-1) is complete (S_X(j) was committed after PV_X(j-1)) and
           // PV_X(j) waits for the arrival below.

@@ -47,8 +47,24 @@ __host__ __device__ inline KeySchedule make_key_schedule(int q0, int len, int sp
   return s;
 }
 
+// Keys of tile j that can hold a kept pair, rounded up to a multiple of 16
+// (the MMA's N granularity): in split mode the last prefix tile stops at
+// `prefix` and the last window tile at the tile's last query; all other
+// tiles are kBlockN wide. Columns past the width are masked anyway (prefix
+// cap or causal bound).
+__host__ __device__ inline int key_tile_width(const KeySchedule& s, int j, int q_last, int prefix);
+
 __host__ __device__ inline int key_tile_start(const KeySchedule& s, int j) {
   return (!s.split || j < s.n_prefix) ? j * kBlockN : s.ws + (j - s.n_prefix) * kBlockN;
+}
+
+__host__ __device__ inline int key_tile_width(const KeySchedule& s, int j, int q_last, int prefix) {
+  if (!s.split) return kBlockN;
+  int rem = kBlockN;
+  if (j < s.n_prefix) rem = prefix - j * kBlockN;
+  else if (j == s.n - 1) rem = q_last - key_tile_start(s, j) + 1;
+  if (rem >= kBlockN) return kBlockN;
+  return ((rem + 15) / 16) * 16;
 }
 
 // Attention kernel arguments besides the three tensor maps.
