@@ -165,6 +165,24 @@ QWA_API qwa_status qwa_attention_noalloc(const void *q, const void *k, const voi
                                          const int32_t *cu_seqlens_host, int batch, int mode,
                                          int prefix, int window, void *stream);
 
+/* Last-token L2 pooling of a packed ragged batch. Replaces poolShader /
+ * LastTokenPoolKernel.createRun (src/webgpu/ops.ts:347-379). hidden: f16
+ * [cu_seqlens[batch], width] row-major; out: f32 [batch, width]; out[b] =
+ * h / sqrt(sum h^2) with h = hidden[cu_seqlens[b+1]-1] (no epsilon, like the
+ * reference: an all-zero row gives non-finite values). An empty request
+ * (cu_seqlens[b+1] == cu_seqlens[b]) gives a zero row. width must be a
+ * positive multiple of 8; hidden and out 16-byte aligned. */
+QWA_API qwa_status qwa_last_token_pool(qwa_ctx *ctx, const void *hidden, int width, float *out,
+                                       const int32_t *cu_seqlens_host, int batch, void *stream);
+
+/* The reference's padded form, LastTokenPoolKernel.createRun(input, lengths,
+ * output, batch, sequence, width) (ops.ts:361-379): lengths is a DEVICE
+ * uint32 [batch] buffer, row b*sequence + lengths[b]-1 is pooled (lengths[b]
+ * <= sequence; larger values are clamped to sequence; 0 gives a zero row). */
+QWA_API qwa_status qwa_last_token_pool_padded(qwa_ctx *ctx, const void *hidden,
+                                              const uint32_t *lengths_device, float *out,
+                                              int batch, int sequence, int width, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -278,3 +278,28 @@ int oracle_threads(void) {
   return 1;
 #endif
 }
+
+/* Last-token L2 pooling, src/webgpu/ops.ts:347-359 (poolShader): request b's
+ * embedding is row cu[b+1]-1 of hidden [T, width] (f16) scaled by
+ * 1/sqrt(sum of squares), computed in fp64 here (the shader sums in f32).
+ * An empty request gives a zero row (the reference never pools one: every
+ * request carries at least its EOS token). */
+void oracle_last_token_pool(const uint16_t *hidden, int width, const int32_t *cu, int batch,
+                            double *out) {
+  init_lut();
+  for (int b = 0; b < batch; ++b) {
+    double *dst = out + (int64_t)b * width;
+    if (cu[b + 1] <= cu[b]) {
+      for (int i = 0; i < width; ++i) dst[i] = 0.0;
+      continue;
+    }
+    const uint16_t *row = hidden + (int64_t)(cu[b + 1] - 1) * width;
+    double ss = 0.0;
+    for (int i = 0; i < width; ++i) {
+      const double x = half_to_double(row[i]);
+      ss += x * x;
+    }
+    const double inv = 1.0 / sqrt(ss);
+    for (int i = 0; i < width; ++i) dst[i] = half_to_double(row[i]) * inv;
+  }
+}

@@ -70,6 +70,7 @@ def lib():
         L.oracle_resolve_sparse.restype = ctypes.c_int
         L.oracle_kept_pairs.argtypes = [ctypes.c_int] * 4
         L.oracle_kept_pairs.restype = ctypes.c_int64
+        L.oracle_last_token_pool.argtypes = [P, ctypes.c_int, P, ctypes.c_int, P]
         L.oracle_threads.restype = ctypes.c_int
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -158,6 +159,18 @@ def c_attention_rows(q, k, v, v_stride: int, v_offset: int, cu_seqlens, rows,
         lib().oracle_attention_rows(_ptr(q), _ptr(k), _ptr(v), v_stride, v_offset, _ptr(cu),
                                     len(cu) - 1, mode, prefix, window, _ptr(rows), len(rows),
                                     _ptr(out))
+    return out
+
+
+def c_last_token_pool(hidden: np.ndarray, cu_seqlens) -> np.ndarray:
+    """src/webgpu/ops.ts:347-359; hidden f16 [T, width]; returns fp64 [B, width]."""
+    hidden = np.ascontiguousarray(hidden)
+    assert hidden.dtype == np.float16 and hidden.ndim == 2
+    cu = _cu(cu_seqlens)
+    batch = len(cu) - 1
+    out = np.zeros((batch, hidden.shape[1]), dtype=np.float64)
+    if batch:
+        lib().oracle_last_token_pool(_ptr(hidden), hidden.shape[1], _ptr(cu), batch, _ptr(out))
     return out
 
 
@@ -256,6 +269,31 @@ def np_attention(q, k, v, v_stride, v_offset, cu_seqlens, mode=MODE_AUTO, prefix
             sc -= sc.max(axis=1, keepdims=True)
             p = np.exp(sc)
             out[s0:s0 + L, h] = (p @ vs) / p.sum(axis=1, keepdims=True)
+    return out
+
+
+def np_last_token_pool(hidden, cu_seqlens) -> np.ndarray:
+    """numpy twin of c_last_token_pool (src/webgpu/ops.ts:347-359)."""
+    cu = np.asarray(cu_seqlens, dtype=np.int64)
+    h = np.asarray(hidden).astype(np.float64)
+    out = np.zeros((len(cu) - 1, h.shape[1]))
+    for b in range(len(cu) - 1):
+        if cu[b + 1] > cu[b]:
+            x = h[cu[b + 1] - 1]
+            out[b] = x / np.sqrt(np.sum(x * x))
+    return out
+
+
+def np_last_token_pool_padded(hidden, lengths, sequence: int) -> np.ndarray:
+    """The reference's padded indexing, row b*sequence + lengths[b]-1
+    (src/webgpu/ops.ts:351), as a twin for the padded entry point."""
+    cu_rows = [b * sequence + int(n) for b, n in enumerate(lengths)]
+    h = np.asarray(hidden).astype(np.float64)
+    out = np.zeros((len(lengths), h.shape[1]))
+    for b, n in enumerate(lengths):
+        if n:
+            x = h[cu_rows[b] - 1]
+            out[b] = x / np.sqrt(np.sum(x * x))
     return out
 
 

@@ -404,6 +404,46 @@ qwa_status qwa_qk_norm_rope_padded(qwa_ctx* ctx, const void* qkv, int64_t qkv_st
                       static_cast<cudaStream_t>(stream));
 }
 
+qwa_status qwa_last_token_pool(qwa_ctx* ctx, const void* hidden, int width, float* out,
+                               const int32_t* cu_seqlens_host, int batch, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int total = 0, max_len = 0;
+  qwa_status st = check_cu(ctx, cu_seqlens_host, batch, &total, &max_len);
+  if (st != QWA_OK) return st;
+  if (width < 8 || width % 8 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "width must be a positive multiple of 8 (got %d)", width);
+  if (!out || (total > 0 && !hidden)) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(out) || (hidden && !aligned16(hidden)))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "hidden and out must be 16-byte aligned");
+  Plan* plan = nullptr;
+  st = get_plan(ctx, cu_seqlens_host, batch, -1, 0, 0, s, &plan);
+  if (st != QWA_OK) return st;
+  QWA_CUDA(ctx, launch_last_token_pool(static_cast<const __half*>(hidden), width, plan->d_cu,
+                                       nullptr, 0, batch, out, s));
+  return QWA_OK;
+}
+
+qwa_status qwa_last_token_pool_padded(qwa_ctx* ctx, const void* hidden,
+                                      const uint32_t* lengths_device, float* out, int batch,
+                                      int sequence, int width, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  if (batch < 1 || sequence < 1)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "batch and sequence must be >= 1");
+  if (width < 8 || width % 8 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "width must be a positive multiple of 8 (got %d)", width);
+  if (!hidden || !lengths_device || !out)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(out) || !aligned16(hidden))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "hidden and out must be 16-byte aligned");
+  QWA_CUDA(ctx, launch_last_token_pool(static_cast<const __half*>(hidden), width, nullptr,
+                                       lengths_device, sequence, batch, out,
+                                       static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
 qwa_status qwa_attention(qwa_ctx* ctx, const void* q, const void* k, const void* v,
                          int64_t v_stride, int64_t v_offset, void* out,
                          const int32_t* cu_seqlens_host, int batch, int mode, int prefix,

@@ -101,4 +101,10 @@ cudaError_t launch_qk_norm_rope(const __half* qkv, int64_t qkv_stride, const flo
                                 __half* k_out, const int32_t* cu_seqlens, int batch, int tokens,
                                 int padded_sequence, float eps, cudaStream_t stream);
 
+// Last-token L2 pool. cu_seqlens != nullptr: request b ends at row
+// cu[b+1]-1; otherwise row b*sequence + lengths[b]-1 (padded layout).
+cudaError_t launch_last_token_pool(const __half* hidden, int width, const int32_t* cu_seqlens,
+                                   const uint32_t* lengths, int sequence, int batch, float* out,
+                                   cudaStream_t stream);
+
 }  // namespace qwa

@@ -106,3 +106,27 @@ def test_kept_pairs_counts(oracle):
     assert oracle.c_kept_pairs(5000, False) == 5000 * 5001 // 2
     assert 16 * oracle.c_kept_pairs(5000, True) == 45_687_552
     assert oracle.resolve_sparse(oracle.MODE_AUTO, 8192) and not oracle.resolve_sparse(0, 8193)
+
+
+def test_last_token_pool_c_matches_numpy(oracle):
+    rng = np.random.default_rng(11)
+    h = rng.standard_normal((300, 1024)).astype(np.float16)
+    cu = [0, 1, 1, 90, 300]
+    a = oracle.c_last_token_pool(h, cu)
+    b = oracle.np_last_token_pool(h, cu)
+    assert np.abs(a - b).max() < 1e-12
+    assert np.allclose(np.linalg.norm(a[[0, 2, 3]], axis=1), 1.0)
+    assert not a[1].any()  # empty request -> zero row
+    # the row pooled is the request's last one (ops.ts:351)
+    x = h[89].astype(np.float64)
+    assert np.allclose(a[2], x / np.linalg.norm(x))
+
+
+def test_last_token_pool_padded_twin_matches_varlen(oracle):
+    rng = np.random.default_rng(12)
+    S, lengths = 40, [3, 40, 17]
+    h = rng.standard_normal((len(lengths) * S, 64)).astype(np.float16)
+    pad = oracle.np_last_token_pool_padded(h, lengths, S)
+    rows = np.concatenate([h[b * S:b * S + n] for b, n in enumerate(lengths)])
+    cu = np.concatenate([[0], np.cumsum(lengths)])
+    assert np.abs(pad - oracle.c_last_token_pool(rows, cu)).max() < 1e-12
