@@ -246,12 +246,20 @@ def run_engine(args):
     run = pool.LastTokenPoolKernel(0).create_run_varlen(hidden, cu, outp)
     for _ in range(10):
         pkg.attention.encode_run(None, run)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # 200 launches captured in one CUDA graph, so the host's submission rate
+    # does not set the time
     n = 200
-    e0.record()
-    for _ in range(n):
-        pkg.attention.encode_run(None, run)
-    e1.record()
+    gs = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
+        for _ in range(n):
+            pkg.attention.encode_run(None, run)
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(gs)
+    graph.replay()
+    e1.record(gs)
     torch.cuda.synchronize()
     pool_ms = e0.elapsed_time(e1) / n
     pool_bytes = len(lengths) * 1024 * (2 + 4)
@@ -271,7 +279,8 @@ def run_engine(args):
         "padded_vs_varlen_min_cosine": float(cos.min()),
         "pool_kernel": {"avg_launch_ms": pool_ms, "bytes_per_launch": pool_bytes,
                         "achieved_gbs": pool_bytes / (pool_ms * 1e-3) / 1e9,
-                        "bound": "launch latency (96 KB per launch)"},
+                        "bound": "launch latency (96 KB per launch)",
+                        "timing": "CUDA graph of 200 back-to-back launches, events"},
         "timing": "wall clock around each whole micro-batch through EmbeddingEngine, "
                   "synchronised; pool kernel by CUDA events",
         "clocks": clocks.summary(),
