@@ -263,6 +263,30 @@ def run_engine(args):
     torch.cuda.synchronize()
     pool_ms = e0.elapsed_time(e1) / n
     pool_bytes = len(lengths) * 1024 * (2 + 4)
+    # residual + RMSNorm over the packed batch: reads x and the residual, writes
+    # x and normalized (8 KB per 1024-wide row; 429 MB per launch, > L2)
+    normm = importlib.import_module(PKG + ".norm")
+    xs = torch.randn(cu[-1], 1024, device="cuda").half()
+    delta = (0.01 * torch.randn(cu[-1], 1024, device="cuda")).half()
+    nw = torch.ones(1024, device="cuda")
+    nout = torch.empty_like(xs)
+    nrun = normm.RmsNormKernel(0).create_run(xs, delta, nw, nout, cu[-1], 1024, 1e-6, True)
+    for _ in range(5):
+        pkg.attention.encode_run(None, nrun)
+    nn = 20
+    ng = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ng, stream=gs):
+        for _ in range(nn):
+            pkg.attention.encode_run(None, nrun)
+    ng.replay()
+    torch.cuda.synchronize()
+    e0.record(gs)
+    ng.replay()
+    e1.record(gs)
+    torch.cuda.synchronize()
+    norm_ms = e0.elapsed_time(e1) / nn
+    norm_bytes = cu[-1] * 1024 * 2 * 4
+    peaks, psrc = measured_peaks()
     v = results["varlen"]
     line = {
         "metric": "embedding micro-batch requests/s (engine, attention stack)",
@@ -271,8 +295,8 @@ def run_engine(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic token ids; random-init weights (seeded)",
         "config": {"workload": "engine_mixed16", "lengths": list(lengths), "layers": L,
-                   "per_layer": "input RMSNorm, QKV GEMM (torch), qk_norm_rope, attention, "
-                                "O GEMM + residual (torch); final RMSNorm; last-token pool",
+                   "per_layer": "QKV GEMM (torch), qk_norm_rope, attention, O GEMM (torch), "
+                                "residual + RMSNorm; then last-token pool",
                    "packing": "varlen"},
         "packing": results,
         "varlen_speedup_over_padded": results["padded"]["ms_per_step"] / v["ms_per_step"],
@@ -281,6 +305,12 @@ def run_engine(args):
                         "achieved_gbs": pool_bytes / (pool_ms * 1e-3) / 1e9,
                         "bound": "launch latency (96 KB per launch)",
                         "timing": "CUDA graph of 200 back-to-back launches, events"},
+        "rms_norm_kernel": {"avg_launch_ms": norm_ms, "rows": cu[-1], "width": 1024,
+                            "bytes_per_launch": norm_bytes,
+                            "achieved_gbs": norm_bytes / (norm_ms * 1e-3) / 1e9,
+                            "peak_gbs": peaks["hbm_gbs"], "peak_source": f"{psrc} hbm_gbs",
+                            "frac": norm_bytes / (norm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                            "timing": "CUDA graph of 20 launches, events; with residual"},
         "timing": "wall clock around each whole micro-batch through EmbeddingEngine, "
                   "synchronised; pool kernel by CUDA events",
         "clocks": clocks.summary(),

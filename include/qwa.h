@@ -183,6 +183,18 @@ QWA_API qwa_status qwa_last_token_pool_padded(qwa_ctx *ctx, const void *hidden,
                                               const uint32_t *lengths_device, float *out,
                                               int batch, int sequence, int width, void *stream);
 
+/* Residual add + RMSNorm of the residual stream. Replaces rmsNormShader /
+ * RmsNormKernel.createRun(x, residual, weight, normalized, rows, width,
+ * epsilon, hasResidual) (src/webgpu/ops.ts:21-64). x, residual, normalized:
+ * f16 [rows, width]; weight: f32 [width]. With has_residual != 0, x is
+ * updated in place to f16(x + residual) and the sum of squares uses the
+ * unrounded f32 sums; normalized = f16(x * 1/sqrt(mean(x^2) + eps) * weight).
+ * width must be a positive multiple of 8; pointers 16-byte aligned; residual
+ * may be NULL when has_residual == 0. */
+QWA_API qwa_status qwa_rms_norm(qwa_ctx *ctx, void *x, const void *residual, const float *weight,
+                                void *normalized, int rows, int width, float eps,
+                                int has_residual, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

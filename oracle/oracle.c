@@ -303,3 +303,63 @@ void oracle_last_token_pool(const uint16_t *hidden, int width, const int32_t *cu
     for (int i = 0; i < width; ++i) dst[i] = half_to_double(row[i]) * inv;
   }
 }
+
+/* f32 -> f16 bits with IEEE round-to-nearest-even (the conversion WGSL's
+ * f16() and CUDA's __float2half_rn perform; floatToHalf in src/math/f16.ts
+ * rounds ties away from zero instead and is only used for host uploads). */
+static uint16_t float_to_half_rne(float value) {
+  uint32_t bits;
+  memcpy(&bits, &value, 4);
+  const uint32_t sign = (bits >> 16) & 0x8000u;
+  const uint32_t absb = bits & 0x7fffffffu;
+  if (absb >= 0x7f800000u) return (uint16_t)(sign | 0x7c00u | (absb > 0x7f800000u ? 0x200u : 0));
+  if (absb >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u); /* rounds to >= 65520: inf */
+  int exponent = (int)(absb >> 23) - 127 + 15;
+  uint32_t mantissa = (absb & 0x7fffffu) | 0x800000u;
+  int shift;
+  if (exponent <= 0) {
+    if (exponent < -10) return (uint16_t)sign;
+    shift = 14 - exponent; /* subnormal: keep 10 bits of m * 2^(e-1) */
+    exponent = 0;
+  } else {
+    shift = 13;
+  }
+  uint32_t kept = mantissa >> shift;
+  const uint32_t rest = mantissa & ((1u << shift) - 1);
+  const uint32_t halfway = 1u << (shift - 1);
+  if (rest > halfway || (rest == halfway && (kept & 1u))) kept += 1;
+  /* kept includes the implicit bit for normals; adding the exponent field
+   * lets a mantissa carry roll into the exponent */
+  uint32_t out = exponent == 0 ? kept : (((uint32_t)(exponent - 1) << 10) + kept);
+  return (uint16_t)(sign | out);
+}
+
+uint16_t oracle_float_to_half_rne(float value) { return float_to_half_rne(value); }
+
+/* Residual add + RMSNorm, src/webgpu/ops.ts:21-57 (rmsNormShader), in the
+ * shader's f32 arithmetic: with residual, v = f32(x) + f32(r) (exact in f32)
+ * and x := f16_rne(v); sum of v^2 (kept in fp64 here, f32 tree in the
+ * shader); inv = 1/sqrt(sum/width + eps); normalized = f16_rne(x*inv*w).
+ * x is updated in place like the shader's read_write binding. */
+void oracle_rms_norm(uint16_t *x, const uint16_t *residual, const float *weight,
+                     uint16_t *normalized, int rows, int width, float eps, int has_residual) {
+  init_lut();
+#pragma omp parallel for schedule(static)
+  for (int row = 0; row < rows; ++row) {
+    uint16_t *xr = x + (int64_t)row * width;
+    const uint16_t *rr = residual ? residual + (int64_t)row * width : NULL;
+    double ss = 0.0;
+    for (int i = 0; i < width; ++i) {
+      float v = (float)half_to_double(xr[i]);
+      if (has_residual) {
+        v += (float)half_to_double(rr[i]);
+        xr[i] = float_to_half_rne(v);
+      }
+      ss += (double)v * (double)v;
+    }
+    const float inv = (float)(1.0 / sqrt(ss / width + (double)eps));
+    uint16_t *nr = normalized + (int64_t)row * width;
+    for (int i = 0; i < width; ++i)
+      nr[i] = float_to_half_rne((float)half_to_double(xr[i]) * inv * weight[i]);
+  }
+}

@@ -71,6 +71,10 @@ def lib():
         L.oracle_kept_pairs.argtypes = [ctypes.c_int] * 4
         L.oracle_kept_pairs.restype = ctypes.c_int64
         L.oracle_last_token_pool.argtypes = [P, ctypes.c_int, P, ctypes.c_int, P]
+        L.oracle_float_to_half_rne.restype = ctypes.c_uint16
+        L.oracle_float_to_half_rne.argtypes = [ctypes.c_float]
+        L.oracle_rms_norm.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                      ctypes.c_int]
         L.oracle_threads.restype = ctypes.c_int
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -174,6 +178,21 @@ def c_last_token_pool(hidden: np.ndarray, cu_seqlens) -> np.ndarray:
     return out
 
 
+def c_rms_norm(x: np.ndarray, residual, weight, eps=1e-6):
+    """src/webgpu/ops.ts:21-57; x/residual f16 [rows, width], weight f32 [width].
+    Returns (x updated by the residual, normalized), both f16."""
+    x = np.array(x, dtype=np.float16, copy=True, order="C")
+    rows, width = x.shape
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    normalized = np.zeros_like(x)
+    r = None if residual is None else np.ascontiguousarray(residual, dtype=np.float16)
+    if rows:
+        lib().oracle_rms_norm(_ptr(x.view(np.uint16)), None if r is None else _ptr(r.view(np.uint16)),
+                              _ptr(w), _ptr(normalized.view(np.uint16)), rows, width, eps,
+                              0 if r is None else 1)
+    return x, normalized
+
+
 def c_kept_pairs(length: int, sparse: bool, prefix=PREFIX, window=WINDOW) -> int:
     return int(lib().oracle_kept_pairs(length, int(sparse), prefix, window))
 
@@ -270,6 +289,18 @@ def np_attention(q, k, v, v_stride, v_offset, cu_seqlens, mode=MODE_AUTO, prefix
             p = np.exp(sc)
             out[s0:s0 + L, h] = (p @ vs) / p.sum(axis=1, keepdims=True)
     return out
+
+
+def np_rms_norm(x, residual, weight, eps=1e-6):
+    """numpy twin of c_rms_norm (float32 elementwise, numpy's RNE casts)."""
+    v = np.asarray(x, dtype=np.float16).astype(np.float32)
+    if residual is not None:
+        v = v + np.asarray(residual, dtype=np.float16).astype(np.float32)
+    xs = v.astype(np.float16)
+    ss = np.sum(v.astype(np.float64) ** 2, axis=1, keepdims=True)
+    inv = (1.0 / np.sqrt(ss / v.shape[1] + eps)).astype(np.float32)
+    w = np.asarray(weight, dtype=np.float32)
+    return xs, (xs.astype(np.float32) * inv * w).astype(np.float16)
 
 
 def np_last_token_pool(hidden, cu_seqlens) -> np.ndarray:

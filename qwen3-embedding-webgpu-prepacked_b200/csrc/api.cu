@@ -404,6 +404,27 @@ qwa_status qwa_qk_norm_rope_padded(qwa_ctx* ctx, const void* qkv, int64_t qkv_st
                       static_cast<cudaStream_t>(stream));
 }
 
+qwa_status qwa_rms_norm(qwa_ctx* ctx, void* x, const void* residual, const float* weight,
+                        void* normalized, int rows, int width, float eps, int has_residual,
+                        void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  if (rows < 0) return fail(ctx, QWA_ERR_INVALID_ARG, "rows must be >= 0");
+  if (width < 8 || width % 8 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "width must be a positive multiple of 8 (got %d)", width);
+  if (!(eps >= 0.f)) return fail(ctx, QWA_ERR_INVALID_ARG, "eps must be >= 0");
+  if (rows == 0) return QWA_OK;
+  if (!x || !weight || !normalized || (has_residual && !residual))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(normalized) ||
+      (has_residual && !aligned16(residual)))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  QWA_CUDA(ctx, launch_rms_norm(static_cast<__half*>(x), static_cast<const __half*>(residual),
+                                weight, static_cast<__half*>(normalized), rows, width,
+                                has_residual != 0, eps, static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
 qwa_status qwa_last_token_pool(qwa_ctx* ctx, const void* hidden, int width, float* out,
                                const int32_t* cu_seqlens_host, int batch, void* stream) {
   if (!ctx) return QWA_ERR_INVALID_ARG;

@@ -107,4 +107,9 @@ cudaError_t launch_last_token_pool(const __half* hidden, int width, const int32_
                                    const uint32_t* lengths, int sequence, int batch, float* out,
                                    cudaStream_t stream);
 
+// Residual add + RMSNorm (ops.ts:21-64); x updated in place when has_residual.
+cudaError_t launch_rms_norm(__half* x, const __half* residual, const float* weight,
+                            __half* normalized, int rows, int width, bool has_residual, float eps,
+                            cudaStream_t stream);
+
 }  // namespace qwa

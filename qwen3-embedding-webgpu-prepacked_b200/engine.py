@@ -26,7 +26,8 @@ Two packings:
   attention pairs) of the packed one.
 
 ``AttentionStackRuntime`` is a device runtime for both packings that runs
-libqwa's kernels (Q/K norm + RoPE, attention, last-token pool) for every layer.
+libqwa's kernels (Q/K norm + RoPE, attention, residual + RMSNorm, last-token
+pool) for every layer.
 """
 from __future__ import annotations
 
@@ -187,14 +188,14 @@ class EmbeddingEngine:
 
 class AttentionStackRuntime:
     """Device runtime for both packings: per layer, the attention half of a
-    Qwen3 block with random-init weights (input RMSNorm, QKV projection, fused
-    Q/K norm + RoPE, attention, output projection + residual), then the final
-    RMSNorm and the last-token L2 pool.
+    Qwen3 block with random-init weights (QKV projection, fused Q/K norm +
+    RoPE, attention, output projection, residual add + RMSNorm with the next
+    layer's weight), then the last-token L2 pool.
 
     The Q/K norm + RoPE, attention and pool steps are libqwa's CUDA kernels;
-    the QKV / output projections and the block RMSNorm are torch (cuBLAS)
-    stand-ins for the Q4_0 matmuls and fused norms that come next, and the MLP
-    is left out. Weights are seeded random (no checkpoint), so the embeddings
+    the residual + RMSNorm steps are libqwa's fused kernel as well; the QKV /
+    output projections are torch (cuBLAS) stand-ins for the Q4_0 matmuls that
+    come next, and the MLP is left out. Weights are seeded random (no checkpoint), so the embeddings
     are not the model's; what this runtime shows is that padded and packed
     batches give the same embedding per request, and what packing saves.
     """
@@ -202,7 +203,9 @@ class AttentionStackRuntime:
     def __init__(self, layers: int = 28, vocab: int = 151669, hidden: int = 1024,
                  device: Optional[int] = None, seed: int = 0):
         from . import attention as attn
+        from . import norm
         self._attn = attn
+        self._norm = norm
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None
                                    else device)
         self.layers = layers
@@ -225,19 +228,20 @@ class AttentionStackRuntime:
                         for _ in range(layers)]
         self.final_norm = (1 + 0.02 * torch.randn(hidden, generator=g, device=dev)).float()
 
-    def _rms(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        xf = x.float()
-        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w).to(torch.float16)
-
     def forward(self, ids: torch.Tensor, cu_seqlens: Sequence[int]) -> torch.Tensor:
-        """Hidden f16 [T, hidden] after the last layer for packed ``ids``."""
-        x = self.embed_table[ids.long()]
+        """Final normalized hidden state f16 [T, hidden] for packed ``ids``,
+        in the encode order of src/webgpu/model.ts:90-104 (FFN left out)."""
+        norm = self._norm
+        x = self.embed_table[ids.long()]  # residual stream, updated in place
+        normalized = norm.rms_norm(x, self.in_norm[0])
         for l in range(self.layers):
-            qkv = self._rms(x, self.in_norm[l]) @ self.w_qkv[l]
+            qkv = normalized @ self.w_qkv[l]
             o = self._attn.prefill_attention_layer(qkv, self.q_norm[l], self.k_norm[l],
                                                    cu_seqlens)
-            x = x + o.view(-1, 2048) @ self.w_o[l]
-        return self._rms(x, self.final_norm)
+            delta = o.view(-1, 2048) @ self.w_o[l]
+            next_w = self.in_norm[l + 1] if l + 1 < self.layers else self.final_norm
+            norm.rms_norm(x, next_w, residual=delta, out=normalized)
+        return normalized
 
     def create_plan(self, batch: int, sequence: int) -> "_PaddedPlan":
         return _PaddedPlan(self, batch, sequence)

@@ -130,3 +130,33 @@ def test_last_token_pool_padded_twin_matches_varlen(oracle):
     rows = np.concatenate([h[b * S:b * S + n] for b, n in enumerate(lengths)])
     cu = np.concatenate([[0], np.cumsum(lengths)])
     assert np.abs(pad - oracle.c_last_token_pool(rows, cu)).max() < 1e-12
+
+
+def test_rne_half_conversion_matches_numpy(oracle):
+    import warnings
+    rng = np.random.default_rng(21)
+    vals = np.concatenate([rng.standard_normal(20000).astype(np.float32) * s
+                           for s in (1e-8, 1e-6, 1e-4, 1.0, 100.0, 6e4)] +
+                          [np.array([65504, 65519.99, 65520, 5.96e-8, 2.98e-8, 2.99e-8, 0.0,
+                                     -0.0, np.inf, -np.inf], np.float32)])
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        ref = vals.astype(np.float16).view(np.uint16)
+    got = np.array([oracle.lib().oracle_float_to_half_rne(float(v)) for v in vals], np.uint16)
+    assert np.array_equal(ref, got)
+
+
+@pytest.mark.parametrize("has_residual", [True, False])
+def test_rms_norm_c_matches_numpy(oracle, has_residual):
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal((40, 1024)).astype(np.float16)
+    r = rng.standard_normal((40, 1024)).astype(np.float16) if has_residual else None
+    w = (1 + 0.02 * rng.standard_normal(1024)).astype(np.float32)
+    cx, cn = oracle.c_rms_norm(x, r, w)
+    nx, nn = oracle.np_rms_norm(x, r, w)
+    assert np.array_equal(cx, nx) and np.array_equal(cn, nn)
+    if not has_residual:
+        assert np.array_equal(cx, x)
+    # RMS of the normalized row (before the weight) is 1
+    rms = np.sqrt(np.mean((cn.astype(np.float64) / w) ** 2, axis=1))
+    assert np.allclose(rms, 1.0, atol=2e-3)
