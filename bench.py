@@ -254,12 +254,13 @@ def run_engine(args):
     with torch.cuda.graph(graph, stream=gs):
         for _ in range(n):
             pkg.attention.encode_run(None, run)
-    graph.replay()
-    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(gs)
-    graph.replay()
-    e1.record(gs)
+    with torch.cuda.stream(gs):  # replay on the stream the events are recorded on
+        graph.replay()
+        torch.cuda.synchronize()
+        e0.record(gs)
+        graph.replay()
+        e1.record(gs)
     torch.cuda.synchronize()
     pool_ms = e0.elapsed_time(e1) / n
     pool_bytes = len(lengths) * 1024 * (2 + 4)
@@ -278,11 +279,12 @@ def run_engine(args):
     with torch.cuda.graph(ng, stream=gs):
         for _ in range(nn):
             pkg.attention.encode_run(None, nrun)
-    ng.replay()
-    torch.cuda.synchronize()
-    e0.record(gs)
-    ng.replay()
-    e1.record(gs)
+    with torch.cuda.stream(gs):
+        ng.replay()
+        torch.cuda.synchronize()
+        e0.record(gs)
+        ng.replay()
+        e1.record(gs)
     torch.cuda.synchronize()
     norm_ms = e0.elapsed_time(e1) / nn
     norm_bytes = cu[-1] * 1024 * 2 * 4
