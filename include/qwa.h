@@ -195,6 +195,35 @@ QWA_API qwa_status qwa_rms_norm(qwa_ctx *ctx, void *x, const void *residual, con
                                 void *normalized, int rows, int width, float eps,
                                 int has_residual, void *stream);
 
+/* Projection GEMM, f16: output[m, n] = sum_k input[m, k] * weight[n, k],
+ * f32 accumulation on the tensor cores, f16 result. input f16 [m, k] and
+ * weight f16 [n, k] row-major, output f16 [m, n] row-major. Replaces the
+ * arithmetic of QuantMatmulKernel (src/webgpu/quant-matmul.ts:495-540) once
+ * the weight is dequantised. n must be a multiple of 256 and k of 64
+ * (QWA_ERR_UNSUPPORTED otherwise); pointers 16-byte aligned. */
+QWA_API qwa_status qwa_matmul(qwa_ctx *ctx, const void *input, const void *weight, void *output,
+                              int m, int n, int k, void *stream);
+
+/* Dequantise a Q4_0 "q4_0-tile32-compact" matrix (src/prepacked/format.ts:
+ * 65-99; values as quant-matmul.ts:98-107, f16(scale) * (q - 8) in f16) to
+ * f16 weight[n, k] row-major. packed: ceil(n/32) * (k/32) * 32 records of 20
+ * bytes, 4-byte aligned; k a multiple of 32. Bit-exact with the reference's
+ * dequantised values. */
+QWA_API qwa_status qwa_q40_dequantize(qwa_ctx *ctx, const void *packed, int n, int k,
+                                      void *weight, void *stream);
+
+/* QuantMatmulKernel.createRunFromBuffers(input, weights, m, n, k, output) +
+ * encode for the prepacked tile32 layout (quant-matmul.ts:495-540): the
+ * first call for a given (packed, n, k) dequantises the matrix into an f16
+ * copy owned by the context (n * k * 2 bytes, kept until qwa_q40_forget or
+ * qwa_destroy); every call then runs qwa_matmul on that copy. A caller that
+ * rewrites the packed buffer in place calls qwa_q40_forget first. */
+QWA_API qwa_status qwa_q40_matmul(qwa_ctx *ctx, const void *input, const void *packed,
+                                  void *output, int m, int n, int k, void *stream);
+
+/* Drop the context's f16 copies made from `packed` (synchronises the device). */
+QWA_API qwa_status qwa_q40_forget(qwa_ctx *ctx, const void *packed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,10 @@ SIGNATURES = {
     "qwa_attention_work": (I32, [I32P, I32, I32, I32, I32, I64P, I64P]),
     "qwa_selftest_tile": (I32, [P, P, P, P, P, P, P]),
     "qwa_attention_noalloc": (I32, [P, P, P, I64, I64, P, I32P, I32, I32, I32, I32, P]),
+    "qwa_matmul": (I32, [P, P, P, P, I32, I32, I32, P]),
+    "qwa_q40_dequantize": (I32, [P, P, I32, I32, P, P]),
+    "qwa_q40_matmul": (I32, [P, P, P, P, I32, I32, I32, P]),
+    "qwa_q40_forget": (I32, [P, P]),
     "qwa_rms_norm": (I32, [P, P, P, P, P, I32, I32, F32, I32, P]),
     "qwa_last_token_pool": (I32, [P, P, I32, P, I32P, I32, P]),
     "qwa_last_token_pool_padded": (I32, [P, P, P, P, I32, I32, I32, P]),

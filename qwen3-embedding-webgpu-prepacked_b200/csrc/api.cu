@@ -18,6 +18,7 @@
 #include <map>
 #include <memory>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "../../include/qwa.h"
@@ -58,6 +59,8 @@ struct qwa_ctx {
   float rope_theta = 0.f;
   std::map<std::vector<int32_t>, std::unique_ptr<Plan>> plans;
   std::vector<std::vector<int32_t>> plan_order;  // insertion order for eviction
+  // f16 weights dequantised from Q4_0 tile32 buffers, keyed by (buffer, n, k)
+  std::map<std::tuple<const void*, int, int>, __half*> weights;
   unsigned long long* trace = nullptr;           // QWA_TRACE builds only
 };
 
@@ -111,6 +114,24 @@ qwa_status make_map(qwa_ctx* ctx, CUtensorMap* map, const void* base, int heads,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(ctx, QWA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return QWA_OK;
+}
+
+// 2-D f16 map {inner, rows} with row stride inner*2 bytes, box {64, box_rows},
+// 128-byte swizzle (one box = box_rows rows x 128 B, the SW128 K-major atom
+// layout the GEMM's descriptors expect). Rows past `rows` read as zero.
+qwa_status make_map_2d(qwa_ctx* ctx, CUtensorMap* map, const void* base, int64_t inner,
+                       int64_t rows, uint32_t box_rows) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner * 2)};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(ctx, QWA_ERR_CUDA, "cuTensorMapEncodeTiled (2-D) failed (%d)", static_cast<int>(r));
   return QWA_OK;
 }
 
@@ -352,6 +373,8 @@ qwa_status qwa_destroy(qwa_ctx* ctx) {
     DeviceGuard guard(ctx->device);
     cudaDeviceSynchronize();
     ctx->plans.clear();
+    for (auto& w : ctx->weights) cudaFree(w.second);
+    ctx->weights.clear();
     if (ctx->d_rope) cudaFree(ctx->d_rope);
     if (ctx->d_status) cudaFree(ctx->d_status);
   }
@@ -402,6 +425,104 @@ qwa_status qwa_qk_norm_rope_padded(qwa_ctx* ctx, const void* qkv, int64_t qkv_st
   return run_prologue(ctx, qkv, qkv_stride, q_weight, k_weight, q_out, k_out, nullptr, 1, tokens,
                       sequence, std::min(sequence, tokens), eps, theta, rope_table,
                       static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+qwa_status check_matmul_shape(qwa_ctx* ctx, int m, int n, int k) {
+  if (m < 0) return fail(ctx, QWA_ERR_INVALID_ARG, "m must be >= 0");
+  if (n < 256 || n % 256 != 0)
+    return fail(ctx, QWA_ERR_UNSUPPORTED, "n must be a positive multiple of 256 (got %d)", n);
+  if (k < 64 || k % 64 != 0)
+    return fail(ctx, QWA_ERR_UNSUPPORTED, "k must be a positive multiple of 64 (got %d)", k);
+  return QWA_OK;
+}
+
+qwa_status run_matmul(qwa_ctx* ctx, const void* input, const void* weight, void* output, int m,
+                      int n, int k, cudaStream_t stream) {
+  if (!input || !weight || !output) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(input) || !aligned16(weight) || !aligned16(output))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  qwa_status st = ensure_encode(ctx);
+  if (st != QWA_OK) return st;
+  CUtensorMap tm_a, tm_w;
+  if ((st = make_map_2d(ctx, &tm_a, input, k, m, 128)) != QWA_OK) return st;
+  if ((st = make_map_2d(ctx, &tm_w, weight, k, n, 256)) != QWA_OK) return st;
+  QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, static_cast<__half*>(output), m, n, k, ctx->d_status,
+                                stream));
+  return QWA_OK;
+}
+
+qwa_status check_q40(qwa_ctx* ctx, const void* packed, int n, int k) {
+  if (!packed) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL weight pointer");
+  if (n < 1 || k < 32 || k % 32 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "n must be >= 1 and k a positive multiple of 32");
+  if (reinterpret_cast<uintptr_t>(packed) & 3u)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "packed weights must be 4-byte aligned");
+  return QWA_OK;
+}
+
+}  // namespace
+
+qwa_status qwa_q40_dequantize(qwa_ctx* ctx, const void* packed, int n, int k, void* weight,
+                              void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  qwa_status st = check_q40(ctx, packed, n, k);
+  if (st != QWA_OK) return st;
+  if (!weight || !aligned16(weight))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "weight must be a 16-byte aligned pointer");
+  QWA_CUDA(ctx, launch_q40_tile32_dequant(static_cast<const uint8_t*>(packed), n, k,
+                                          static_cast<__half*>(weight),
+                                          static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
+qwa_status qwa_matmul(qwa_ctx* ctx, const void* input, const void* weight, void* output, int m,
+                      int n, int k, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  qwa_status st = check_matmul_shape(ctx, m, n, k);
+  if (st != QWA_OK) return st;
+  if (m == 0) return QWA_OK;
+  return run_matmul(ctx, input, weight, output, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
+qwa_status qwa_q40_matmul(qwa_ctx* ctx, const void* input, const void* packed, void* output,
+                          int m, int n, int k, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  qwa_status st = check_matmul_shape(ctx, m, n, k);
+  if (st == QWA_OK) st = check_q40(ctx, packed, n, k);
+  if (st != QWA_OK) return st;
+  const auto key = std::make_tuple(packed, n, k);
+  auto it = ctx->weights.find(key);
+  __half* w = nullptr;
+  if (it == ctx->weights.end()) {
+    QWA_CUDA(ctx, cudaMalloc(&w, static_cast<size_t>(n) * k * sizeof(__half)));
+    ctx->weights[key] = w;
+    QWA_CUDA(ctx, launch_q40_tile32_dequant(static_cast<const uint8_t*>(packed), n, k, w, s));
+  } else {
+    w = it->second;
+  }
+  if (m == 0) return QWA_OK;
+  return run_matmul(ctx, input, w, output, m, n, k, s);
+}
+
+qwa_status qwa_q40_forget(qwa_ctx* ctx, const void* packed) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  QWA_CUDA(ctx, cudaDeviceSynchronize());
+  for (auto it = ctx->weights.begin(); it != ctx->weights.end();) {
+    if (std::get<0>(it->first) == packed) {
+      cudaFree(it->second);
+      it = ctx->weights.erase(it);
+    } else {
+      ++it;
+    }
+  }
+  return QWA_OK;
 }
 
 qwa_status qwa_rms_norm(qwa_ctx* ctx, void* x, const void* residual, const float* weight,

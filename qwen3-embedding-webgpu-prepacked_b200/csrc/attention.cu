@@ -589,21 +589,23 @@ __global__ void __launch_bounds__(128, 1)
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const AttnArgs& args, int num_items,
                              cudaStream_t stream) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  // function attributes and SM counts are per device
+  static bool configured[kMaxDevices] = {};
+  static int sms[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[dev] = true;
   }
   if (num_items <= 0) return cudaSuccess;
-  static int sm_count = 0;
-  if (!sm_count) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-  }
+  const int sm_count = sms[dev];
   const int grid = num_items < sm_count ? num_items : sm_count;  // persistent: one CTA per SM
   attention_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, args, num_items);
   return cudaGetLastError();

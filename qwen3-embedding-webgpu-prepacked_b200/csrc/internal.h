@@ -107,6 +107,19 @@ cudaError_t launch_last_token_pool(const __half* hidden, int width, const int32_
                                    const uint32_t* lengths, int sequence, int batch, float* out,
                                    cudaStream_t stream);
 
+constexpr int kMaxDevices = 64;
+
+// C[M,N] = A[M,K] W[N,K]^T, f16 in/out, f32 accumulate (tcgen05). tm_a: 2-D
+// map {K, M} box {64, 128}; tm_w: {K, N} box {64, 256}; 128-byte swizzle.
+// N % 256 == 0, K % 64 == 0.
+cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
+                            int N, int K, int* status, cudaStream_t stream);
+
+// Q4_0 tile32-compact records (20 bytes: f16 scale, 2 pad bytes, 16 bytes of
+// nibbles) -> f16 W[n, k] row-major.
+cudaError_t launch_q40_tile32_dequant(const uint8_t* packed, int n, int k, __half* out,
+                                      cudaStream_t stream);
+
 // Residual add + RMSNorm (ops.ts:21-64); x updated in place when has_residual.
 cudaError_t launch_rms_norm(__half* x, const __half* residual, const float* weight,
                             __half* normalized, int rows, int width, bool has_residual, float eps,

@@ -38,7 +38,6 @@ namespace {
 constexpr size_t kScratchBytes = 1u << 20;  // 1 MiB
 constexpr size_t kStatusBytes = 256;        // status word, padded
 constexpr size_t kMaxItems = (kScratchBytes - kStatusBytes) / sizeof(AttnItem);
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 

@@ -21,6 +21,10 @@ enum DeviceError : int {
   kDevTimeoutSFull = 0x104,
   kDevTimeoutPFull = 0x105,
   kDevTimeoutOFinal = 0x106,
+  kDevTimeoutGemmEmpty = 0x201,
+  kDevTimeoutGemmFull = 0x202,
+  kDevTimeoutAccEmpty = 0x203,
+  kDevTimeoutAccFull = 0x204,
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -92,6 +96,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// 2-D tiled TMA load (c0 innermost, in elements; c0*2 bytes a multiple of 16).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
 

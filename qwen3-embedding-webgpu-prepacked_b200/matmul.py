@@ -1,0 +1,104 @@
+"""Projection matmuls: Q4_0 tile32 weights on the tensor cores.
+
+Mirrors ``QuantMatmulKernel`` for the prepacked layout
+(src/webgpu/quant-matmul.ts:453-540): ``create_run_from_buffers(input,
+weights, m, n, k, output)`` binds a run computing ``output[m, n] = sum_k
+input[m, k] * W[n, k]`` where W is the Q4_0 "q4_0-tile32-compact" matrix in
+``weights`` (src/prepacked/format.ts:65-99), and ``encode(stream, run)``
+issues it. On B200 the matrix is dequantised once to an f16 copy (bit-exact
+with the reference's dequantised values) and every run is a tcgen05 GEMM with
+f32 accumulation (csrc/gemm.cu); the reference accumulates in f16.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .attention import Context, _need, _ptr, _stream
+
+LAYOUT_TILE32 = "q4_0-tile32-compact"
+
+
+def packed_bytes(n: int, k: int) -> int:
+    """Size of a tile32-compact matrix: ceil(n/32) * (k/32) * 32 records of 20 B."""
+    return (n + 31) // 32 * (k // 32) * 32 * 20
+
+
+def _f16(t: torch.Tensor, name: str, numel: int) -> None:
+    _need(isinstance(t, torch.Tensor) and t.is_cuda and t.dtype == torch.float16
+          and t.is_contiguous() and t.numel() >= numel,
+          f"{name} must be a contiguous CUDA float16 tensor of at least {numel} elements")
+
+
+@dataclass
+class QuantMatmulRun:
+    """quant-matmul.ts:442-451 (input, weights, output, m, n, k)."""
+    input: torch.Tensor
+    weights: torch.Tensor
+    output: torch.Tensor
+    m: int
+    n: int
+    k: int
+
+
+class QuantMatmulKernel:
+    """quant-matmul.ts:453 -- prepacked tile32 Q4_0 only (GGUF Q4_K/Q6_K are
+    outside the attention path)."""
+
+    def __init__(self, device=None, layout: str = LAYOUT_TILE32):
+        if layout != LAYOUT_TILE32:
+            raise ValueError("only the q4_0-tile32-compact layout is supported")
+        self.ctx = Context.for_device(device)
+        self.layout = layout
+
+    def create_run_from_buffers(self, input: torch.Tensor, weights: torch.Tensor, m: int, n: int,
+                                k: int, output: Optional[torch.Tensor] = None) -> QuantMatmulRun:
+        _f16(input, "input", m * k)
+        _need(weights.is_cuda and weights.dtype == torch.uint8 and weights.is_contiguous()
+              and weights.numel() >= packed_bytes(n, k),
+              "weights must be a contiguous CUDA uint8 tile32-compact buffer")
+        if output is None:
+            output = torch.empty(m, n, dtype=torch.float16, device=input.device)
+        _f16(output, "output", m * n)
+        return QuantMatmulRun(input, weights, output, m, n, k)
+
+    def encode(self, stream, run: QuantMatmulRun) -> None:
+        st = self.ctx.lib.qwa_q40_matmul(self.ctx.handle, _ptr(run.input), _ptr(run.weights),
+                                         _ptr(run.output), run.m, run.n, run.k, _stream(stream))
+        _lib.check(st, self.ctx.handle)
+
+    def forget(self, weights: torch.Tensor) -> None:
+        """Drop the f16 copy made from ``weights`` (after rewriting it in place)."""
+        _lib.check(self.ctx.lib.qwa_q40_forget(self.ctx.handle, _ptr(weights)), self.ctx.handle)
+
+
+def q40_dequantize(packed: torch.Tensor, n: int, k: int, out: Optional[torch.Tensor] = None,
+                   stream=None) -> torch.Tensor:
+    """f16 W [n, k] from a tile32-compact buffer."""
+    _need(packed.is_cuda and packed.dtype == torch.uint8 and packed.numel() >= packed_bytes(n, k),
+          "packed must be a CUDA uint8 tile32-compact buffer")
+    out = out if out is not None else torch.empty(n, k, dtype=torch.float16, device=packed.device)
+    _f16(out, "out", n * k)
+    ctx = Context.for_device(packed.device.index)
+    _lib.check(ctx.lib.qwa_q40_dequantize(ctx.handle, _ptr(packed), n, k, _ptr(out),
+                                          _stream(stream)), ctx.handle)
+    return out
+
+
+def matmul(input: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor] = None,
+           stream=None) -> torch.Tensor:
+    """f16 [m, n] = input [m, k] @ weight [n, k]^T on the tensor cores."""
+    m, k = input.shape
+    n = weight.shape[0]
+    _f16(input, "input", m * k)
+    _f16(weight, "weight", n * k)
+    out = out if out is not None else torch.empty(m, n, dtype=torch.float16, device=input.device)
+    _f16(out, "out", m * n)
+    ctx = Context.for_device(input.device.index)
+    _lib.check(ctx.lib.qwa_matmul(ctx.handle, _ptr(input), _ptr(weight), _ptr(out), m, n, k,
+                                  _stream(stream)), ctx.handle)
+    return out

@@ -1,0 +1,87 @@
+"""Q4_0 tile32 dequantisation and the tcgen05 projection GEMM vs the oracle.
+
+Dequantisation is bit-exact (f16 products, round to nearest even). The GEMM
+accumulates in f32 and rounds once to f16; against the fp64 oracle each
+element must satisfy |got - ref| <= 1e-3 * |ref| + 2e-3 * max|ref| (f16
+output rounding plus f32 accumulation over up to 3072 terms), and every row
+must have cosine >= 0.99999 with the oracle.
+"""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q40
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(got: np.ndarray, ref: np.ndarray):
+    got = got.astype(np.float64)
+    scale = np.abs(ref).max()
+    assert np.all(np.abs(got - ref) <= 1e-3 * np.abs(ref) + 2e-3 * scale), \
+        float(np.abs(got - ref).max() / scale)
+    cos = np.sum(got * ref, 1) / (np.linalg.norm(got, axis=1) * np.linalg.norm(ref, axis=1) + 1e-30)
+    assert cos.min() >= 0.99999
+
+
+def _packed(rng, n, k):
+    rows = q40.random_q40_rows(rng, n, k)
+    packed, _, _ = q40.pack_q40_tile32([(rows, n)])
+    return packed
+
+
+@pytest.mark.parametrize("n,k", [(4096, 1024), (1000, 64), (31, 2048)])
+def test_dequant_bit_exact(pkg, cuda_dev, n, k):
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(n + k)
+    packed = _packed(rng, n, k)
+    got = mm.q40_dequantize(torch.from_numpy(packed).cuda(), n, k).cpu().numpy()
+    ref = q40.dequant_tile32(packed, n, k)
+    assert np.array_equal(got.view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (1, 256, 64), (50, 1024, 1024), (128, 4096, 1024), (1000, 1024, 2048),
+    (777, 512, 3072), (5000, 4096, 1024), (300, 6144, 1024),
+])
+def test_matmul_matches_oracle(pkg, cuda_dev, m, n, k):
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(m * 31 + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    w = (rng.standard_normal((n, k)) * k ** -0.5).astype(np.float16)
+    got = mm.matmul(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda())
+    pkg.attention.Context.for_device(0).check()
+    _check(got.cpu().numpy(), q40.matmul(a, w))
+
+
+def test_q40_matmul_run_matches_oracle_and_caches(pkg, cuda_dev):
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(7)
+    m, n, k = 640, 4096, 1024
+    packed = _packed(rng, n, k)
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    kern = mm.QuantMatmulKernel(0)
+    dp = torch.from_numpy(packed).cuda()
+    run = kern.create_run_from_buffers(torch.from_numpy(a).cuda(), dp, m, n, k)
+    kern.encode(None, run)
+    first = run.output.clone()
+    kern.encode(None, run)  # served from the cached f16 copy
+    assert torch.equal(first, run.output)
+    _check(run.output.cpu().numpy(), q40.matmul(a, q40.dequant_tile32(packed, n, k)))
+    # rewriting the packed buffer needs forget(); then the new values are used
+    dp.zero_()
+    kern.forget(dp)
+    kern.encode(None, run)
+    assert not run.output.any()
+
+
+def test_matmul_rejects_unsupported_shapes(pkg, cuda_dev):
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    a = torch.zeros(4, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(Exception):
+        mm.matmul(a, torch.zeros(100, 64, dtype=torch.float16, device="cuda"))
+    with pytest.raises(Exception):
+        mm.matmul(torch.zeros(4, 40, dtype=torch.float16, device="cuda"),
+                  torch.zeros(256, 40, dtype=torch.float16, device="cuda"))
