@@ -295,10 +295,10 @@ def run_engine(args):
         "value": v["requests_per_s"], "unit": "requests/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": v["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic token ids; random-init weights (seeded)",
+        "data": "synthetic token ids; seeded random Q4_0 tile32 weights",
         "config": {"workload": "engine_mixed16", "lengths": list(lengths), "layers": L,
-                   "per_layer": "QKV GEMM (torch), qk_norm_rope, attention, O GEMM (torch), "
-                                "residual + RMSNorm; then last-token pool",
+                   "per_layer": "Q4_0 QKV projection (tcgen05 GEMM), qk_norm_rope, attention, "
+                                "Q4_0 O projection, residual + RMSNorm; then last-token pool",
                    "packing": "varlen"},
         "packing": results,
         "varlen_speedup_over_padded": results["padded"]["ms_per_step"] / v["ms_per_step"],

@@ -188,22 +188,23 @@ class EmbeddingEngine:
 
 class AttentionStackRuntime:
     """Device runtime for both packings: per layer, the attention half of a
-    Qwen3 block with random-init weights (QKV projection, fused Q/K norm +
-    RoPE, attention, output projection, residual add + RMSNorm with the next
-    layer's weight), then the last-token L2 pool.
+    Qwen3 block with seeded synthetic weights, in the encode order of
+    src/webgpu/model.ts:90-104 without the FFN -- QKV projection, fused Q/K
+    norm + RoPE, attention, output projection, residual add + RMSNorm with
+    the next layer's weight -- then the last-token L2 pool. Every step is a
+    libqwa kernel: the projections take Q4_0 tile32-compact matrices (as the
+    prepacked model stores attn_qkv / attn_output) through QuantMatmulKernel,
+    which dequantises each once and runs the tcgen05 GEMM.
 
-    The Q/K norm + RoPE, attention and pool steps are libqwa's CUDA kernels;
-    the residual + RMSNorm steps are libqwa's fused kernel as well; the QKV /
-    output projections are torch (cuBLAS) stand-ins for the Q4_0 matmuls that
-    come next, and the MLP is left out. Weights are seeded random (no checkpoint), so the embeddings
-    are not the model's; what this runtime shows is that padded and packed
-    batches give the same embedding per request, and what packing saves.
+    Weights are seeded random (no checkpoint), so the embeddings are not the
+    model's; what this runtime shows is that padded and packed batches give
+    the same embedding per request, and what packing saves.
     """
 
     def __init__(self, layers: int = 28, vocab: int = 151669, hidden: int = 1024,
                  device: Optional[int] = None, seed: int = 0):
         from . import attention as attn
-        from . import norm
+        from . import matmul, norm, prepacked
         self._attn = attn
         self._norm = norm
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None
@@ -211,34 +212,44 @@ class AttentionStackRuntime:
         self.layers = layers
         self.vocab = vocab
         self.hidden = hidden
+        self.q40 = matmul.QuantMatmulKernel(self.device.index)
         g = torch.Generator(device=self.device).manual_seed(seed)
-        dev, f16 = self.device, torch.float16
+        rng = np.random.default_rng(seed)
+        dev = self.device
 
-        def rnd(*shape, scale):
-            return (torch.randn(*shape, generator=g, device=dev) * scale).to(f16)
+        def packed(n: int, k: int, scale: float) -> torch.Tensor:
+            rows = prepacked.random_q40_rows(rng, n, k, scale)
+            t = prepacked.pack_q40_tile32("w", [prepacked.q40_part("w", rows, k)])
+            return torch.from_numpy(t.bytes).to(dev)
 
-        self.embed_table = rnd(vocab, hidden, scale=1.0)
-        self.w_qkv = [rnd(hidden, 4096, scale=hidden ** -0.5) for _ in range(layers)]
-        self.w_o = [rnd(2048, hidden, scale=2048 ** -0.5) for _ in range(layers)]
-        self.q_norm = [(1 + 0.02 * torch.randn(128, generator=g, device=dev)).float()
-                       for _ in range(layers)]
-        self.k_norm = [(1 + 0.02 * torch.randn(128, generator=g, device=dev)).float()
-                       for _ in range(layers)]
-        self.in_norm = [(1 + 0.02 * torch.randn(hidden, generator=g, device=dev)).float()
-                        for _ in range(layers)]
-        self.final_norm = (1 + 0.02 * torch.randn(hidden, generator=g, device=dev)).float()
+        def gains(n: int) -> torch.Tensor:
+            return (1 + 0.02 * torch.randn(n, generator=g, device=dev)).float()
+
+        self.embed_table = torch.randn(vocab, hidden, generator=g, device=dev).half()
+        # Q4_0 values are scale * (q - 8), q uniform: std ~ 4.6 * scale
+        self.w_qkv = [packed(4096, hidden, 0.2 / hidden ** 0.5) for _ in range(layers)]
+        self.w_o = [packed(hidden, 2048, 0.2 / 2048 ** 0.5) for _ in range(layers)]
+        self.q_norm = [gains(128) for _ in range(layers)]
+        self.k_norm = [gains(128) for _ in range(layers)]
+        self.in_norm = [gains(hidden) for _ in range(layers)]
+        self.final_norm = gains(hidden)
+
+    def _project(self, x: torch.Tensor, w: torch.Tensor, n: int) -> torch.Tensor:
+        m, k = x.shape
+        run = self.q40.create_run_from_buffers(x, w, m, n, k)
+        self.q40.encode(None, run)
+        return run.output
 
     def forward(self, ids: torch.Tensor, cu_seqlens: Sequence[int]) -> torch.Tensor:
-        """Final normalized hidden state f16 [T, hidden] for packed ``ids``,
-        in the encode order of src/webgpu/model.ts:90-104 (FFN left out)."""
+        """Final normalized hidden state f16 [T, hidden] for packed ``ids``."""
         norm = self._norm
         x = self.embed_table[ids.long()]  # residual stream, updated in place
         normalized = norm.rms_norm(x, self.in_norm[0])
         for l in range(self.layers):
-            qkv = normalized @ self.w_qkv[l]
+            qkv = self._project(normalized, self.w_qkv[l], 4096)
             o = self._attn.prefill_attention_layer(qkv, self.q_norm[l], self.k_norm[l],
                                                    cu_seqlens)
-            delta = o.view(-1, 2048) @ self.w_o[l]
+            delta = self._project(o.view(-1, 2048), self.w_o[l], self.hidden)
             next_w = self.in_norm[l + 1] if l + 1 < self.layers else self.final_norm
             norm.rms_norm(x, next_w, residual=delta, out=normalized)
         return normalized
