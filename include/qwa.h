@@ -221,6 +221,32 @@ QWA_API qwa_status qwa_q40_dequantize(qwa_ctx *ctx, const void *packed, int n, i
 QWA_API qwa_status qwa_q40_matmul(qwa_ctx *ctx, const void *input, const void *packed,
                                   void *output, int m, int n, int k, void *stream);
 
+/* attn_qkv projection fused with the per-head Q/K RMSNorm + RoPE: the
+ * matmul(normalized, attn_qkv) + QKNormRopeKernel pair of src/webgpu/
+ * model.ts:93-94 (ops.ts:104-166) in one launch. input f16 [T, k] (T =
+ * cu_seqlens[batch], requests packed back to back), weight f16 [4096, k]
+ * (rows 0..2047 q, 2048..3071 k, 3072..4095 v); writes q f16 [T,16,128] and
+ * k f16 [T,8,128] normalised and rotated at each token's position inside its
+ * request, and v f16 [T,1024] (pass v_stride 1024, v_offset 0 to
+ * qwa_attention). The qkv values are rounded to f16 before the norm exactly
+ * as the unfused path stores qkvRaw, and the norm / rotation arithmetic is
+ * the prologue's, so results equal qwa_matmul + qwa_qk_norm_rope bit for bit.
+ * rope_table as for qwa_qk_norm_rope (NULL: the context's table for theta).
+ * k must be a multiple of 64. */
+QWA_API qwa_status qwa_qkv_projection(qwa_ctx *ctx, const void *input, const void *weight, int k,
+                                      const float *q_weight, const float *k_weight, void *q_out,
+                                      void *k_out, void *v_out, const int32_t *cu_seqlens_host,
+                                      int batch, float eps, float theta, const float *rope_table,
+                                      void *stream);
+
+/* qwa_qkv_projection with the weight as a Q4_0 tile32-compact matrix [4096, k]
+ * (dequantised once into the context's cache, as qwa_q40_matmul). */
+QWA_API qwa_status qwa_q40_qkv_projection(qwa_ctx *ctx, const void *input, const void *packed,
+                                          int k, const float *q_weight, const float *k_weight,
+                                          void *q_out, void *k_out, void *v_out,
+                                          const int32_t *cu_seqlens_host, int batch, float eps,
+                                          float theta, const float *rope_table, void *stream);
+
 /* Drop the context's f16 copies made from `packed` (synchronises the device). */
 QWA_API qwa_status qwa_q40_forget(qwa_ctx *ctx, const void *packed);
 

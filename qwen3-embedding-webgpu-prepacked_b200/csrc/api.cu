@@ -488,6 +488,97 @@ qwa_status qwa_matmul(qwa_ctx* ctx, const void* input, const void* weight, void*
   return run_matmul(ctx, input, weight, output, m, n, k, static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+
+// f16 copy of a Q4_0 tile32 matrix owned by the context (made on first use).
+qwa_status cached_q40(qwa_ctx* ctx, const void* packed, int n, int k, cudaStream_t s,
+                      __half** out) {
+  const auto key = std::make_tuple(packed, n, k);
+  auto it = ctx->weights.find(key);
+  if (it != ctx->weights.end()) {
+    *out = it->second;
+    return QWA_OK;
+  }
+  __half* w = nullptr;
+  QWA_CUDA(ctx, cudaMalloc(&w, static_cast<size_t>(n) * k * sizeof(__half)));
+  ctx->weights[key] = w;
+  QWA_CUDA(ctx, launch_q40_tile32_dequant(static_cast<const uint8_t*>(packed), n, k, w, s));
+  *out = w;
+  return QWA_OK;
+}
+
+qwa_status run_qkv_projection(qwa_ctx* ctx, const void* input, const void* weight, int k,
+                              const float* q_weight, const float* k_weight, void* q_out,
+                              void* k_out, void* v_out, const int32_t* cu, int batch, float eps,
+                              float theta, const float* rope_table, cudaStream_t s) {
+  int total = 0, max_len = 0;
+  qwa_status st = check_cu(ctx, cu, batch, &total, &max_len);
+  if (st != QWA_OK) return st;
+  if (k < 64 || k % 64 != 0)
+    return fail(ctx, QWA_ERR_UNSUPPORTED, "k must be a positive multiple of 64 (got %d)", k);
+  if (!(eps >= 0.f)) return fail(ctx, QWA_ERR_INVALID_ARG, "eps must be >= 0");
+  if (total == 0) return QWA_OK;
+  if (!input || !weight || !q_weight || !k_weight || !q_out || !k_out || !v_out)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(input) || !aligned16(weight) || !aligned16(q_weight) || !aligned16(k_weight) ||
+      !aligned16(q_out) || !aligned16(k_out) || !aligned16(v_out) ||
+      (rope_table && !aligned16(rope_table)))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  if ((st = ensure_encode(ctx)) != QWA_OK) return st;
+  Plan* plan = nullptr;
+  if ((st = get_plan(ctx, cu, batch, -1, 0, 0, s, &plan)) != QWA_OK) return st;
+  const float* table = rope_table;
+  if (!table) {
+    if ((st = ensure_rope(ctx, max_len, theta, s)) != QWA_OK) return st;
+    table = ctx->d_rope;
+  }
+  CUtensorMap tm_a, tm_w;
+  if ((st = make_map_2d(ctx, &tm_a, input, k, total, 128)) != QWA_OK) return st;
+  if ((st = make_map_2d(ctx, &tm_w, weight, k, 4096, 256)) != QWA_OK) return st;
+  QkvEpilogue e;
+  e.q_out = static_cast<__half*>(q_out);
+  e.k_out = static_cast<__half*>(k_out);
+  e.v_out = static_cast<__half*>(v_out);
+  e.q_weight = q_weight;
+  e.k_weight = k_weight;
+  e.table = reinterpret_cast<const float2*>(table);
+  e.cu = plan->d_cu;
+  e.batch = batch;
+  e.eps = eps;
+  QWA_CUDA(ctx, launch_gemm_qkv(tm_a, tm_w, total, k, e, ctx->d_status, s));
+  return QWA_OK;
+}
+
+}  // namespace
+
+qwa_status qwa_qkv_projection(qwa_ctx* ctx, const void* input, const void* weight, int k,
+                              const float* q_weight, const float* k_weight, void* q_out,
+                              void* k_out, void* v_out, const int32_t* cu_seqlens_host,
+                              int batch, float eps, float theta, const float* rope_table,
+                              void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  return run_qkv_projection(ctx, input, weight, k, q_weight, k_weight, q_out, k_out, v_out,
+                            cu_seqlens_host, batch, eps, theta, rope_table,
+                            static_cast<cudaStream_t>(stream));
+}
+
+qwa_status qwa_q40_qkv_projection(qwa_ctx* ctx, const void* input, const void* packed, int k,
+                                  const float* q_weight, const float* k_weight, void* q_out,
+                                  void* k_out, void* v_out, const int32_t* cu_seqlens_host,
+                                  int batch, float eps, float theta, const float* rope_table,
+                                  void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  qwa_status st = check_q40(ctx, packed, 4096, k);
+  if (st != QWA_OK) return st;
+  __half* w = nullptr;
+  if ((st = cached_q40(ctx, packed, 4096, k, s, &w)) != QWA_OK) return st;
+  return run_qkv_projection(ctx, input, w, k, q_weight, k_weight, q_out, k_out, v_out,
+                            cu_seqlens_host, batch, eps, theta, rope_table, s);
+}
+
 qwa_status qwa_q40_matmul(qwa_ctx* ctx, const void* input, const void* packed, void* output,
                           int m, int n, int k, void* stream) {
   if (!ctx) return QWA_ERR_INVALID_ARG;
@@ -496,16 +587,8 @@ qwa_status qwa_q40_matmul(qwa_ctx* ctx, const void* input, const void* packed, v
   qwa_status st = check_matmul_shape(ctx, m, n, k);
   if (st == QWA_OK) st = check_q40(ctx, packed, n, k);
   if (st != QWA_OK) return st;
-  const auto key = std::make_tuple(packed, n, k);
-  auto it = ctx->weights.find(key);
   __half* w = nullptr;
-  if (it == ctx->weights.end()) {
-    QWA_CUDA(ctx, cudaMalloc(&w, static_cast<size_t>(n) * k * sizeof(__half)));
-    ctx->weights[key] = w;
-    QWA_CUDA(ctx, launch_q40_tile32_dequant(static_cast<const uint8_t*>(packed), n, k, w, s));
-  } else {
-    w = it->second;
-  }
+  if ((st = cached_q40(ctx, packed, n, k, s, &w)) != QWA_OK) return st;
   if (m == 0) return QWA_OK;
   return run_matmul(ctx, input, w, output, m, n, k, s);
 }

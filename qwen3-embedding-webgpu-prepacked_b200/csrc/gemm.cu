@@ -13,6 +13,15 @@
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row),
 //               f32 -> f16, 16-byte stores; releases the accumulator so the
 //               MMAs of the next tile overlap this tile's stores.
+// With the QKV epilogue (N = 4096, the attn_qkv projection of
+// src/webgpu/model.ts:93), a 256-column tile holds two whole heads of each
+// row, so the epilogue thread of a row also applies the per-head Q/K RMSNorm
+// + RoPE of qkNormRopeShader (src/webgpu/ops.ts:104-150) to the q and k
+// tiles and writes q [T,16,128], k [T,8,128] and v [T,8,128] directly: the
+// [T, 4096] qkvRaw round trip and the separate prologue launch disappear.
+// The arithmetic is the unfused pipeline's, step for step (accumulator
+// rounded to f16 as qkvRaw would be, the prologue kernel's f32 sum order,
+// normalisation and rotation), so both paths give identical bits.
 // Output tiles are walked n-fastest so consecutive tiles of a CTA (and the
 // CTAs running at the same time) share the A rows in L2; W (<= 12 MB for
 // Qwen3-0.6B) stays L2-resident.
@@ -38,10 +47,79 @@ constexpr uint32_t kGemmSmem = kAbortOff + 4 + 1024;  // + alignment slack
 static_assert(kGemmSmem <= 232448, "shared memory budget");
 constexpr uint32_t kIdesc = idesc_f16_f32(kBM, kBN, false);
 
+__device__ __forceinline__ int request_start(const int32_t* cu, int batch, int t) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(cu + mid) <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  return __ldg(cu + lo);
+}
+
+// One head (128 accumulator columns at t_head) of one row: f16-round, RMSNorm
+// with weight w, NEOX RoPE at position pos, 256-byte store to dst.
+__device__ __forceinline__ void norm_rope_head(uint32_t t_head, const float* __restrict__ w,
+                                               const float4* __restrict__ trow, float eps,
+                                               bool valid, __half* dst) {
+  uint32_t h[64];  // the head's 128 values as packed f16 pairs
+  float part[16];  // sums of squares of dims 8j .. 8j+7
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[32];
+    tmem_ld32(t_head + 32 * c, v);
+    tmem_wait_ld();
+    reg_fence32(v);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) h[16 * c + i] = pack_half2(__uint_as_float(v[2 * i]),
+                                                            __uint_as_float(v[2 * i + 1]));
+  }
+  if (!valid) return;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[4 * j + e]));
+      s = fmaf(f.x, f.x, s);
+      s = fmaf(f.y, f.y, s);
+    }
+    part[j] = s;
+  }
+  // the prologue's 16-lane butterfly (xor 8, 4, 2, 1), pair by pair
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[j] = part[j] + part[j + 8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) part[j] = part[j] + part[j + 4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) part[j] = part[j] + part[j + 2];
+  const float ss = part[0] + part[1];
+  const float inv = 1.0f / sqrtf(ss * (1.0f / 128) + eps);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {  // dims 8q .. 8q+7 and 64+8q .. 64+8q+7
+    uint32_t lo_out[4], hi_out[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = 8 * q + 2 * e;
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h[d / 2]));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&h[32 + d / 2]));
+      const float4 cs = __ldg(trow + d / 2);  // (cos, sin) of dims d, d+1
+      const float na0 = a.x * inv * __ldg(w + d), na1 = a.y * inv * __ldg(w + d + 1);
+      const float nb0 = b.x * inv * __ldg(w + 64 + d), nb1 = b.y * inv * __ldg(w + 65 + d);
+      lo_out[e] = pack_half2(fmaf(na0, cs.x, -1.f * nb0 * cs.y), fmaf(na1, cs.z, -1.f * nb1 * cs.w));
+      hi_out[e] = pack_half2(fmaf(nb0, cs.x, 1.f * na0 * cs.y), fmaf(nb1, cs.z, 1.f * na1 * cs.w));
+    }
+    d4[q] = make_uint4(lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
+    d4[8 + q] = make_uint4(hi_out[0], hi_out[1], hi_out[2], hi_out[3]);
+  }
+}
+
+template <bool kQkv>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_w, __half* __restrict__ out, int M,
-                    int N, int K, int* status) {
+                    int N, int K, int* status, const QkvEpilogue qkv) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -140,22 +218,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t t_row = tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * kBN;
       const int row = m0 + r;
-      uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * N + n0);
+      const int nt = n0 / kBN;
+      if (kQkv && nt < 12) {
+        // q tiles 0..7 (heads 2nt, 2nt+1), k tiles 8..11 (kv heads 2(nt-8), +1)
+        const bool is_q = nt < 8;
+        const bool valid = row < M;
+        const int pos = valid ? row - request_start(qkv.cu, qkv.batch, row) : 0;
+        const float4* trow = reinterpret_cast<const float4*>(qkv.table + static_cast<int64_t>(pos) * 64);
+        const float* w = is_q ? qkv.q_weight : qkv.k_weight;
+        const int head0 = is_q ? 2 * nt : 2 * (nt - 8);
+        __half* base = is_q ? qkv.q_out + (static_cast<int64_t>(row) * 16 + head0) * 128
+                            : qkv.k_out + (static_cast<int64_t>(row) * 8 + head0) * 128;
 #pragma unroll 1
-      for (int ch = 0; ch < kBN / 32; ++ch) {
-        uint32_t v[32];
-        tmem_ld32(t_row + 32 * ch, v);
-        tmem_wait_ld();
-        reg_fence32(v);
-        if (row < M) {
+        for (int hh = 0; hh < 2; ++hh)
+          norm_rope_head(t_row + 128 * hh, w, trow, qkv.eps, valid, base + 128 * hh);
+      } else {
+        __half* orow;
+        int64_t stride;
+        if (kQkv) {  // v tiles 12..15 -> v [T, 1024]
+          orow = qkv.v_out + static_cast<int64_t>(row) * 1024 + (n0 - 3072);
+          stride = 1024;
+        } else {
+          orow = out + static_cast<int64_t>(row) * N + n0;
+          stride = N;
+        }
+        (void)stride;
+        uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll 1
+        for (int ch = 0; ch < kBN / 32; ++ch) {
+          uint32_t v[32];
+          tmem_ld32(t_row + 32 * ch, v);
+          tmem_wait_ld();
+          reg_fence32(v);
+          if (row < M) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
-            w.y = pack_half2(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
-            w.z = pack_half2(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
-            w.w = pack_half2(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
-            dst[4 * ch + q] = w;
+            for (int q = 0; q < 4; ++q) {
+              uint4 wv;
+              wv.x = pack_half2(__uint_as_float(v[8 * q + 0]), __uint_as_float(v[8 * q + 1]));
+              wv.y = pack_half2(__uint_as_float(v[8 * q + 2]), __uint_as_float(v[8 * q + 3]));
+              wv.z = pack_half2(__uint_as_float(v[8 * q + 4]), __uint_as_float(v[8 * q + 5]));
+              wv.w = pack_half2(__uint_as_float(v[8 * q + 6]), __uint_as_float(v[8 * q + 7]));
+              dst[4 * ch + q] = wv;
+            }
           }
         }
       }
@@ -172,10 +276,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-}  // namespace
-
-cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
-                            int N, int K, int* status, cudaStream_t stream) {
+template <bool kQkv>
+cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
+                        int N, int K, int* status, const QkvEpilogue& qkv, cudaStream_t stream) {
   static bool configured[kMaxDevices] = {};
   static int sm_count[kMaxDevices] = {};
   int dev = 0;
@@ -183,7 +286,7 @@ cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_f16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gemm_f16_kernel<kQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kGemmSmem);
     if (e == cudaSuccess)
       e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -194,8 +297,21 @@ cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __
   const int tiles = ((M + kBM - 1) / kBM) * (N / kBN);
   const int grid = tiles < sms ? tiles : sms;
   if (grid <= 0) return cudaSuccess;
-  gemm_f16_kernel<<<grid, kGemmThreads, kGemmSmem, stream>>>(tm_a, tm_w, out, M, N, K, status);
+  gemm_f16_kernel<kQkv><<<grid, kGemmThreads, kGemmSmem, stream>>>(tm_a, tm_w, out, M, N, K,
+                                                                   status, qkv);
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
+                            int N, int K, int* status, cudaStream_t stream) {
+  return launch_gemm<false>(tm_a, tm_w, out, M, N, K, status, QkvEpilogue{}, stream);
+}
+
+cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
+                            const QkvEpilogue& qkv, int* status, cudaStream_t stream) {
+  return launch_gemm<true>(tm_a, tm_w, nullptr, M, 4096, K, status, qkv, stream);
 }
 
 }  // namespace qwa

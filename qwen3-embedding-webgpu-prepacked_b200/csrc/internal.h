@@ -115,6 +115,24 @@ constexpr int kMaxDevices = 64;
 cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
                             int N, int K, int* status, cudaStream_t stream);
 
+// Fused attn_qkv projection epilogue: per-head Q/K RMSNorm + RoPE on the q/k
+// tiles, v written as [T, 1024]. Positions are row - cu[request(row)].
+struct QkvEpilogue {
+  __half* q_out = nullptr;  // [T, 16, 128]
+  __half* k_out = nullptr;  // [T, 8, 128]
+  __half* v_out = nullptr;  // [T, 1024]
+  const float* q_weight = nullptr;
+  const float* k_weight = nullptr;
+  const float2* table = nullptr;  // (cos, sin) [positions, 64]
+  const int32_t* cu = nullptr;    // device cu_seqlens [batch + 1]
+  int batch = 0;
+  float eps = 0.f;
+};
+
+// QKV projection (N = 4096) with the QkvEpilogue; K % 64 == 0.
+cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
+                            const QkvEpilogue& qkv, int* status, cudaStream_t stream);
+
 // Q4_0 tile32-compact records (20 bytes: f16 scale, 2 pad bytes, 16 bytes of
 // nibbles) -> f16 W[n, k] row-major.
 cudaError_t launch_q40_tile32_dequant(const uint8_t* packed, int n, int k, __half* out,

@@ -102,3 +102,40 @@ def matmul(input: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor
     _lib.check(ctx.lib.qwa_matmul(ctx.handle, _ptr(input), _ptr(weight), _ptr(out), m, n, k,
                                   _stream(stream)), ctx.handle)
     return out
+
+
+def qkv_projection(input: torch.Tensor, weight: torch.Tensor, q_weight: torch.Tensor,
+                   k_weight: torch.Tensor, cu_seqlens, eps: float = 1e-6, theta: float = 1e6,
+                   q_out: Optional[torch.Tensor] = None, k_out: Optional[torch.Tensor] = None,
+                   v_out: Optional[torch.Tensor] = None, rope_table: Optional[torch.Tensor] = None,
+                   stream=None):
+    """attn_qkv projection fused with the per-head Q/K RMSNorm + RoPE
+    (src/webgpu/model.ts:93-94). ``weight`` is f16 [4096, k] or a uint8 Q4_0
+    tile32-compact buffer; returns (q [T,16,128], k [T,8,128], v [T,1024])."""
+    T, k = input.shape
+    _need(T == int(cu_seqlens[-1]), "input rows must equal cu_seqlens[-1]")
+    _f16(input, "input", T * k)
+    dev = input.device
+    q_out = q_out if q_out is not None else torch.empty(T, 16, 128, dtype=torch.float16, device=dev)
+    k_out = k_out if k_out is not None else torch.empty(T, 8, 128, dtype=torch.float16, device=dev)
+    v_out = v_out if v_out is not None else torch.empty(T, 1024, dtype=torch.float16, device=dev)
+    _f16(q_out, "q_out", T * 2048)
+    _f16(k_out, "k_out", T * 1024)
+    _f16(v_out, "v_out", T * 1024)
+    for t, name in ((q_weight, "q_weight"), (k_weight, "k_weight")):
+        _need(t.is_cuda and t.dtype == torch.float32 and t.numel() == 128 and t.is_contiguous(),
+              f"{name} must be a contiguous CUDA float32 tensor of 128 elements")
+    ctx = Context.for_device(dev.index)
+    cu = _lib.cu_array(cu_seqlens)
+    if weight.dtype == torch.uint8:
+        _need(weight.is_cuda and weight.numel() >= packed_bytes(4096, k),
+              "packed weight must be a CUDA tile32-compact buffer of [4096, k]")
+        fn = ctx.lib.qwa_q40_qkv_projection
+    else:
+        _f16(weight, "weight", 4096 * k)
+        fn = ctx.lib.qwa_qkv_projection
+    st = fn(ctx.handle, _ptr(input), _ptr(weight), k, _ptr(q_weight), _ptr(k_weight),
+            _ptr(q_out), _ptr(k_out), _ptr(v_out), cu, len(cu) - 1, eps, theta,
+            _ptr(rope_table), _stream(stream))
+    _lib.check(st, ctx.handle)
+    return q_out, k_out, v_out

@@ -85,3 +85,52 @@ def test_matmul_rejects_unsupported_shapes(pkg, cuda_dev):
     with pytest.raises(Exception):
         mm.matmul(torch.zeros(4, 40, dtype=torch.float16, device="cuda"),
                   torch.zeros(256, 40, dtype=torch.float16, device="cuda"))
+
+
+@pytest.mark.parametrize("lengths,k", [([50, 17, 130], 1024), ([1], 64), ([5000, 128, 1], 1024),
+                                       ([300, 0, 257], 2048)])
+def test_fused_qkv_projection_equals_unfused_bits(pkg, cuda_dev, lengths, k):
+    """GEMM + rounding to f16 + prologue, fused, must give the unfused bits."""
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    attn = pkg.attention
+    rng = np.random.default_rng(sum(lengths) + k)
+    cu = [0] + [int(c) for c in np.cumsum(lengths)]
+    T = cu[-1]
+    x = torch.from_numpy(rng.standard_normal((T, k)).astype(np.float16)).cuda()
+    w = torch.from_numpy((rng.standard_normal((4096, k)) * k ** -0.5).astype(np.float16)).cuda()
+    qw = torch.from_numpy((1 + 0.02 * rng.standard_normal(128)).astype(np.float32)).cuda()
+    kw = torch.from_numpy((1 + 0.02 * rng.standard_normal(128)).astype(np.float32)).cuda()
+    q, kk, v = mm.qkv_projection(x, w, qw, kw, cu)
+    qkv = mm.matmul(x, w)
+    q_ref, k_ref = attn.qk_norm_rope(qkv, qw, kw, cu)
+    attn.Context.for_device(0).check()
+    assert torch.equal(q.view(torch.int16), q_ref.view(torch.int16))
+    assert torch.equal(kk.view(torch.int16), k_ref.view(torch.int16))
+    assert torch.equal(v, qkv[:, 3072:])
+
+
+def test_fused_qkv_projection_q40_matches_oracle(pkg, oracle, cuda_dev):
+    """Q4_0 weights through the fused kernel vs the CPU oracle (dequantise,
+    fp64 matmul rounded to f16, C prologue). The kernel's f32 accumulation can
+    round a qkvRaw value to the neighbouring f16, so the bound per element is
+    2e-3 plus one f16 ulp of the value (2^-10 |ref|); per-head cosine >= 0.9999."""
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(77)
+    lengths = [50, 17, 130]
+    cu = [0] + [int(c) for c in np.cumsum(lengths)]
+    T, k = cu[-1], 1024
+    packed = _packed(rng, 4096, k)
+    x = rng.standard_normal((T, k)).astype(np.float16)
+    qw = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    kw = (1 + 0.02 * rng.standard_normal(128)).astype(np.float32)
+    q, kk, v = mm.qkv_projection(torch.from_numpy(x).cuda(), torch.from_numpy(packed).cuda(),
+                                 torch.from_numpy(qw).cuda(), torch.from_numpy(kw).cuda(), cu)
+    w = q40.dequant_tile32(packed, 4096, k)
+    qkv = q40.matmul(x, w).astype(np.float16)
+    q_ref, k_ref = oracle.c_qk_norm_rope(qkv, qw, kw, cu)
+    for got, ref in ((q.cpu().numpy().astype(np.float64), q_ref),
+                     (kk.cpu().numpy().astype(np.float64), k_ref)):
+        assert np.all(np.abs(got - ref) <= 2e-3 + np.abs(ref) * 2.0 ** -10)
+        cos = np.sum(got * ref, -1) / (np.linalg.norm(got, axis=-1) * np.linalg.norm(ref, axis=-1))
+        assert cos.min() >= 0.9999
+    _check(v.cpu().numpy(), q40.matmul(x, w)[:, 3072:])
