@@ -297,8 +297,9 @@ def run_engine(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic token ids; seeded random Q4_0 tile32 weights",
         "config": {"workload": "engine_mixed16", "lengths": list(lengths), "layers": L,
-                   "per_layer": "Q4_0 QKV projection (tcgen05 GEMM), qk_norm_rope, attention, "
-                                "Q4_0 O projection, residual + RMSNorm; then last-token pool",
+                   "per_layer": "Q4_0 QKV projection with fused Q/K norm + RoPE (tcgen05), "
+                                "attention, Q4_0 O projection, residual + RMSNorm; then "
+                                "last-token pool",
                    "packing": "varlen"},
         "packing": results,
         "varlen_speedup_over_padded": results["padded"]["ms_per_step"] / v["ms_per_step"],

@@ -189,12 +189,12 @@ class EmbeddingEngine:
 class AttentionStackRuntime:
     """Device runtime for both packings: per layer, the attention half of a
     Qwen3 block with seeded synthetic weights, in the encode order of
-    src/webgpu/model.ts:90-104 without the FFN -- QKV projection, fused Q/K
-    norm + RoPE, attention, output projection, residual add + RMSNorm with
-    the next layer's weight -- then the last-token L2 pool. Every step is a
-    libqwa kernel: the projections take Q4_0 tile32-compact matrices (as the
-    prepacked model stores attn_qkv / attn_output) through QuantMatmulKernel,
-    which dequantises each once and runs the tcgen05 GEMM.
+    src/webgpu/model.ts:90-104 without the FFN -- QKV projection with the
+    Q/K norm + RoPE fused into its epilogue, attention, output projection,
+    residual add + RMSNorm with the next layer's weight -- then the last-token
+    L2 pool. Every step is a libqwa kernel: the projections take Q4_0
+    tile32-compact matrices (as the prepacked model stores attn_qkv /
+    attn_output), dequantised once, on the tcgen05 GEMM.
 
     Weights are seeded random (no checkpoint), so the embeddings are not the
     model's; what this runtime shows is that padded and packed batches give
@@ -207,6 +207,7 @@ class AttentionStackRuntime:
         from . import matmul, norm, prepacked
         self._attn = attn
         self._norm = norm
+        self._matmul = matmul
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None
                                    else device)
         self.layers = layers
@@ -246,9 +247,10 @@ class AttentionStackRuntime:
         x = self.embed_table[ids.long()]  # residual stream, updated in place
         normalized = norm.rms_norm(x, self.in_norm[0])
         for l in range(self.layers):
-            qkv = self._project(normalized, self.w_qkv[l], 4096)
-            o = self._attn.prefill_attention_layer(qkv, self.q_norm[l], self.k_norm[l],
-                                                   cu_seqlens)
+            # attn_qkv projection fused with the Q/K norm + RoPE (one launch)
+            q, k, v = self._matmul.qkv_projection(normalized, self.w_qkv[l], self.q_norm[l],
+                                                  self.k_norm[l], cu_seqlens)
+            o = self._attn.attention(q, k, v, cu_seqlens, value_stride=1024, value_offset=0)
             delta = self._project(o.view(-1, 2048), self.w_o[l], self.hidden)
             next_w = self.in_norm[l + 1] if l + 1 < self.layers else self.final_norm
             norm.rms_norm(x, next_w, residual=delta, out=normalized)
