@@ -5,14 +5,15 @@
 // multiplies `input` [m, k] by the Q4_0 matrix whose row n holds output
 // column n, i.e. output[m, n] = sum_k input[m, k] * W[n, k].
 //
-// Persistent kernel, one CTA per SM, 192 threads:
+// Persistent kernel, one CTA per SM, 320 threads:
 //   warp 0      TMA producer: A tile 128 x 64 and W tile 256 x 64 per stage
 //               (128-byte swizzle), 4-stage ring;
 //   warp 1      TMEM owner and single MMA issuer: per stage 4 x
 //               tcgen05.mma M=128 N=256 K=16 into one of two accumulators;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (thread = row),
-//               f32 -> f16, 16-byte stores; releases the accumulator so the
-//               MMAs of the next tile overlap this tile's stores.
+//   warps 2..9  epilogue: tcgen05.ld of the accumulator (thread = row; the
+//               two warps of a TMEM sub-partition take one 128-column half
+//               each), f32 -> f16, 16-byte stores; releases the accumulator
+//               so the MMAs of the next tile overlap this tile's stores.
 // With the QKV epilogue (N = 4096, the attn_qkv projection of
 // src/webgpu/model.ts:93), a 256-column tile holds two whole heads of each
 // row, so the epilogue thread of a row also applies the per-head Q/K RMSNorm
@@ -33,7 +34,8 @@ namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kStages = 4;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kEpiThreads = 256;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
 constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -41,7 +43,8 @@ constexpr uint32_t kBarOff = kStages * kStageBytes;  // 192 KB
 // barriers: full[4], empty[4], acc_full[2], acc_empty[2]
 constexpr int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2;
 constexpr int kNumBars = 2 * kStages + 4;
-constexpr uint32_t kHolderOff = kBarOff + 8 * kNumBars;
+constexpr uint32_t kNormWOff = kBarOff + 8 * kNumBars;  // q / k norm weights, 2 x 128 f32
+constexpr uint32_t kHolderOff = kNormWOff + 2 * 128 * 4;
 constexpr uint32_t kAbortOff = kHolderOff + 4;
 constexpr uint32_t kGemmSmem = kAbortOff + 4 + 1024;  // + alignment slack
 static_assert(kGemmSmem <= 232448, "shared memory budget");
@@ -58,12 +61,15 @@ __device__ __forceinline__ int request_start(const int32_t* cu, int batch, int t
 }
 
 // One head (128 accumulator columns at t_head) of one row: f16-round, RMSNorm
-// with weight w, NEOX RoPE at position pos, 256-byte store to dst.
-__device__ __forceinline__ void norm_rope_head(uint32_t t_head, const float* __restrict__ w,
+// with weight w (shared memory), NEOX RoPE at the row's table row, 256-byte
+// store to dst. Pass 1 reads the 128 columns for the sum of squares; pass 2
+// re-reads them as the RoPE pairs (d, d + 64).
+__device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
+
+__device__ __forceinline__ void norm_rope_head(uint32_t t_head, const float* w,
                                                const float4* __restrict__ trow, float eps,
                                                bool valid, __half* dst) {
-  uint32_t h[64];  // the head's 128 values as packed f16 pairs
-  float part[16];  // sums of squares of dims 8j .. 8j+7
+  float part[16];  // sums of squares of dims 8j .. 8j+7, as the prologue's lanes
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t v[32];
@@ -71,20 +77,15 @@ __device__ __forceinline__ void norm_rope_head(uint32_t t_head, const float* __r
     tmem_wait_ld();
     reg_fence32(v);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) h[16 * c + i] = pack_half2(__uint_as_float(v[2 * i]),
-                                                            __uint_as_float(v[2 * i + 1]));
-  }
-  if (!valid) return;
+    for (int j = 0; j < 4; ++j) {
+      float sacc = 0.f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    float s = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[4 * j + e]));
-      s = fmaf(f.x, f.x, s);
-      s = fmaf(f.y, f.y, s);
+      for (int e = 0; e < 8; ++e) {
+        const float x = f16_round(__uint_as_float(v[8 * j + e]));
+        sacc = fmaf(x, x, sacc);
+      }
+      part[4 * c + j] = sacc;
     }
-    part[j] = s;
   }
   // the prologue's 16-lane butterfly (xor 8, 4, 2, 1), pair by pair
 #pragma unroll
@@ -96,22 +97,33 @@ __device__ __forceinline__ void norm_rope_head(uint32_t t_head, const float* __r
   const float ss = part[0] + part[1];
   const float inv = 1.0f / sqrtf(ss * (1.0f / 128) + eps);
   uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {  // dims 32c .. 32c+31 with their partners 64 + ...
+    uint32_t lo[32], hi[32];
+    tmem_ld32(t_head + 32 * c, lo);
+    tmem_ld32(t_head + 64 + 32 * c, hi);
+    tmem_wait_ld();
+    reg_fence32(lo);
+    reg_fence32(hi);
+    if (!valid) continue;
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {  // dims 8q .. 8q+7 and 64+8q .. 64+8q+7
-    uint32_t lo_out[4], hi_out[4];
+    for (int q = 0; q < 4; ++q) {  // 8 dims per 16-byte store
+      uint32_t lo_out[4], hi_out[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = 8 * q + 2 * e;
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h[d / 2]));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&h[32 + d / 2]));
-      const float4 cs = __ldg(trow + d / 2);  // (cos, sin) of dims d, d+1
-      const float na0 = a.x * inv * __ldg(w + d), na1 = a.y * inv * __ldg(w + d + 1);
-      const float nb0 = b.x * inv * __ldg(w + 64 + d), nb1 = b.y * inv * __ldg(w + 65 + d);
-      lo_out[e] = pack_half2(fmaf(na0, cs.x, -1.f * nb0 * cs.y), fmaf(na1, cs.z, -1.f * nb1 * cs.w));
-      hi_out[e] = pack_half2(fmaf(nb0, cs.x, 1.f * na0 * cs.y), fmaf(nb1, cs.z, 1.f * na1 * cs.w));
+      for (int e = 0; e < 4; ++e) {
+        const int i = 8 * q + 2 * e;  // index inside the chunk
+        const int d = 32 * c + i;     // dim in [0, 64)
+        const float4 cs = __ldg(trow + d / 2);  // (cos, sin) of dims d, d+1
+        const float na0 = f16_round(__uint_as_float(lo[i])) * inv * w[d];
+        const float na1 = f16_round(__uint_as_float(lo[i + 1])) * inv * w[d + 1];
+        const float nb0 = f16_round(__uint_as_float(hi[i])) * inv * w[64 + d];
+        const float nb1 = f16_round(__uint_as_float(hi[i + 1])) * inv * w[65 + d];
+        lo_out[e] = pack_half2(fmaf(na0, cs.x, -1.f * nb0 * cs.y), fmaf(na1, cs.z, -1.f * nb1 * cs.w));
+        hi_out[e] = pack_half2(fmaf(nb0, cs.x, 1.f * na0 * cs.y), fmaf(nb1, cs.z, 1.f * na1 * cs.w));
+      }
+      d4[4 * c + q] = make_uint4(lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
+      d4[8 + 4 * c + q] = make_uint4(hi_out[0], hi_out[1], hi_out[2], hi_out[3]);
     }
-    d4[q] = make_uint4(lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
-    d4[8 + q] = make_uint4(hi_out[0], hi_out[1], hi_out[2], hi_out[3]);
   }
 }
 
@@ -136,12 +148,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar(kAccFull + a), 1);
-      mbar_init(bar(kAccEmpty + a), 128);
+      mbar_init(bar(kAccEmpty + a), kEpiThreads);
     }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_w);
+  }
+  float* norm_w = reinterpret_cast<float*>(smem + kNormWOff);
+  if (kQkv) {
+    for (int i = threadIdx.x; i < 256; i += kGemmThreads)
+      norm_w[i] = i < 128 ? qkv.q_weight[i] : qkv.k_weight[i - 128];
   }
   if (warp == 1) {
     tmem_alloc(smem_addr(holder), 512);
@@ -204,8 +221,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its sub-partition)
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its sub-partition);
+    // warps 2..5 take columns 0..127 of the tile, warps 6..9 columns 128..255
     const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = sub * 32 + lane;
     bool ok = true;
     int lt = 0;
@@ -216,7 +235,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            kDevTimeoutAccFull)))
         break;
       tc_fence_after();
-      const uint32_t t_row = tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * kBN;
+      const uint32_t t_cols =
+          tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * kBN + 128 * half;
       const int row = m0 + r;
       const int nt = n0 / kBN;
       if (kQkv && nt < 12) {
@@ -224,30 +244,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool is_q = nt < 8;
         const bool valid = row < M;
         const int pos = valid ? row - request_start(qkv.cu, qkv.batch, row) : 0;
-        const float4* trow = reinterpret_cast<const float4*>(qkv.table + static_cast<int64_t>(pos) * 64);
-        const float* w = is_q ? qkv.q_weight : qkv.k_weight;
-        const int head0 = is_q ? 2 * nt : 2 * (nt - 8);
-        __half* base = is_q ? qkv.q_out + (static_cast<int64_t>(row) * 16 + head0) * 128
-                            : qkv.k_out + (static_cast<int64_t>(row) * 8 + head0) * 128;
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh)
-          norm_rope_head(t_row + 128 * hh, w, trow, qkv.eps, valid, base + 128 * hh);
+        const float4* trow =
+            reinterpret_cast<const float4*>(qkv.table + static_cast<int64_t>(pos) * 64);
+        const int head = (is_q ? 2 * nt : 2 * (nt - 8)) + half;
+        __half* dst = is_q ? qkv.q_out + (static_cast<int64_t>(row) * 16 + head) * 128
+                           : qkv.k_out + (static_cast<int64_t>(row) * 8 + head) * 128;
+        norm_rope_head(t_cols, norm_w + (is_q ? 0 : 128), trow, qkv.eps, valid, dst);
       } else {
-        __half* orow;
-        int64_t stride;
-        if (kQkv) {  // v tiles 12..15 -> v [T, 1024]
-          orow = qkv.v_out + static_cast<int64_t>(row) * 1024 + (n0 - 3072);
-          stride = 1024;
-        } else {
-          orow = out + static_cast<int64_t>(row) * N + n0;
-          stride = N;
-        }
-        (void)stride;
-        uint4* dst = reinterpret_cast<uint4*>(orow);
+        __half* orow = kQkv ? qkv.v_out + static_cast<int64_t>(row) * 1024 + (n0 - 3072)
+                            : out + static_cast<int64_t>(row) * N + n0;
+        uint4* dst = reinterpret_cast<uint4*>(orow + 128 * half);
 #pragma unroll 1
-        for (int ch = 0; ch < kBN / 32; ++ch) {
+        for (int ch = 0; ch < 4; ++ch) {
           uint32_t v[32];
-          tmem_ld32(t_row + 32 * ch, v);
+          tmem_ld32(t_cols + 32 * ch, v);
           tmem_wait_ld();
           reg_fence32(v);
           if (row < M) {
