@@ -34,6 +34,7 @@ namespace {
 
 constexpr int kBM = 128, kBN = 256, kBK = 64;
 constexpr int kStages = 4;
+constexpr int kCuSmem = 1024;  // requests whose cu_seqlens are staged in shared memory
 constexpr int kGemmThreads = 320;
 constexpr int kEpiThreads = 256;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
@@ -44,76 +45,87 @@ constexpr uint32_t kBarOff = kStages * kStageBytes;  // 192 KB
 constexpr int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2;
 constexpr int kNumBars = 2 * kStages + 4;
 constexpr uint32_t kNormWOff = kBarOff + 8 * kNumBars;  // q / k norm weights, 2 x 128 f32
-constexpr uint32_t kHolderOff = kNormWOff + 2 * 128 * 4;
+constexpr uint32_t kCuOff = kNormWOff + 2 * 128 * 4;       // cu_seqlens, kCuSmem + 1 ints
+constexpr uint32_t kXchOff = kCuOff + (kCuSmem + 4) * 4;    // norm partial sums, 8 KB
+constexpr uint32_t kPairOkOff = kXchOff + 4 * 2 * 2 * 128 * 4;  // 8 ints
+constexpr uint32_t kHolderOff = kPairOkOff + 8 * 4;
 constexpr uint32_t kAbortOff = kHolderOff + 4;
 constexpr uint32_t kGemmSmem = kAbortOff + 4 + 1024;  // + alignment slack
 static_assert(kGemmSmem <= 232448, "shared memory budget");
 constexpr uint32_t kIdesc = idesc_f16_f32(kBM, kBN, false);
 
+// Start row of the request holding row t: binary search over cu[0..batch].
 __device__ __forceinline__ int request_start(const int32_t* cu, int batch, int t) {
   int lo = 0, hi = batch - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (__ldg(cu + mid) <= t) lo = mid;
+    if (cu[mid] <= t) lo = mid;
     else hi = mid - 1;
   }
-  return __ldg(cu + lo);
+  return cu[lo];
 }
 
-// One head (128 accumulator columns at t_head) of one row: f16-round, RMSNorm
-// with weight w (shared memory), NEOX RoPE at the row's table row, 256-byte
-// store to dst. Pass 1 reads the 128 columns for the sum of squares; pass 2
-// re-reads them as the RoPE pairs (d, d + 64).
 __device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
 
-__device__ __forceinline__ void norm_rope_head(uint32_t t_head, const float* w,
-                                               const float4* __restrict__ trow, float eps,
-                                               bool valid, __half* dst) {
-  float part[16];  // sums of squares of dims 8j .. 8j+7, as the prologue's lanes
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t v[32];
-    tmem_ld32(t_head + 32 * c, v);
-    tmem_wait_ld();
-    reg_fence32(v);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float sacc = 0.f;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float x = f16_round(__uint_as_float(v[8 * j + e]));
-        sacc = fmaf(x, x, sacc);
-      }
-      part[4 * c + j] = sacc;
-    }
-  }
-  // the prologue's 16-lane butterfly (xor 8, 4, 2, 1), pair by pair
-#pragma unroll
-  for (int j = 0; j < 8; ++j) part[j] = part[j] + part[j + 8];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) part[j] = part[j] + part[j + 4];
-#pragma unroll
-  for (int j = 0; j < 2; ++j) part[j] = part[j] + part[j + 2];
-  const float ss = part[0] + part[1];
-  const float inv = 1.0f / sqrtf(ss * (1.0f / 128) + eps);
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ void pair_sync(int sub) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + sub) : "memory");
+}
+
+// Q/K norm + RoPE of one row of a q or k tile, for the quarter of each head
+// this warp owns. The two warps of a TMEM sub-partition split every head's
+// 128 dims: warp c (0 or 1) takes dims [32c, 32c+32) and their RoPE partners
+// [64+32c, 96+32c), so it needs only table entries [32c, 32c+32) of the row
+// (16 float4, loaded once for both heads). Per head the warps exchange the
+// four first-level sums of squares through shared memory; the sum is then
+// combined in the order of the prologue kernel's butterfly (dims in groups of
+// 8, xor 8, 4, 2, 1), so inv equals the prologue's bit for bit.
+__device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int sub, int lane,
+                                                  const float* w, const float4 (&tab)[16],
+                                                  float eps, bool valid, float* xch,
+                                                  __half* dst0) {
 #pragma unroll 1
-  for (int c = 0; c < 2; ++c) {  // dims 32c .. 32c+31 with their partners 64 + ...
+  for (int hh = 0; hh < 2; ++hh) {
     uint32_t lo[32], hi[32];
-    tmem_ld32(t_head + 32 * c, lo);
-    tmem_ld32(t_head + 64 + 32 * c, hi);
+    tmem_ld32(t_tile + 128 * hh + 32 * c, lo);
+    tmem_ld32(t_tile + 128 * hh + 64 + 32 * c, hi);
     tmem_wait_ld();
     reg_fence32(lo);
     reg_fence32(hi);
+    // first level: groups j (dims 8j..8j+7) = 4c..4c+3 and 8+4c..; l1[i] = p[4c+i] + p[8+4c+i]
+    float l1[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float sa = 0.f, sb = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float xa = f16_round(__uint_as_float(lo[8 * i + e]));
+        const float xb = f16_round(__uint_as_float(hi[8 * i + e]));
+        sa = fmaf(xa, xa, sa);
+        sb = fmaf(xb, xb, sb);
+      }
+      l1[i] = sa + sb;
+    }
+    float* mine = xch + ((sub * 2 + hh) * 2 + c) * 128 + lane * 4;
+    float* other = xch + ((sub * 2 + hh) * 2 + (c ^ 1)) * 128 + lane * 4;
+    *reinterpret_cast<float4*>(mine) = make_float4(l1[0], l1[1], l1[2], l1[3]);
+    pair_sync(sub);
+    const float4 o = *reinterpret_cast<const float4*>(other);
+    // second level: groups j < 4 (warp 0's) + groups j + 4 (warp 1's)
+    const float4 g0 = c == 0 ? make_float4(l1[0], l1[1], l1[2], l1[3]) : o;
+    const float4 g1 = c == 0 ? o : make_float4(l1[0], l1[1], l1[2], l1[3]);
+    const float m0 = g0.x + g1.x, m1 = g0.y + g1.y, m2 = g0.z + g1.z, m3 = g0.w + g1.w;
+    const float ss = (m0 + m2) + (m1 + m3);
+    const float inv = 1.0f / sqrtf(ss * (1.0f / 128) + eps);
     if (!valid) continue;
+    uint4* d4 = reinterpret_cast<uint4*>(dst0 + 128 * hh);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // 8 dims per 16-byte store
       uint32_t lo_out[4], hi_out[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int i = 8 * q + 2 * e;  // index inside the chunk
+        const int i = 8 * q + 2 * e;  // index inside the quarter
         const int d = 32 * c + i;     // dim in [0, 64)
-        const float4 cs = __ldg(trow + d / 2);  // (cos, sin) of dims d, d+1
+        const float4 cs = tab[i / 2];  // (cos, sin) of dims d, d+1
         const float na0 = f16_round(__uint_as_float(lo[i])) * inv * w[d];
         const float na1 = f16_round(__uint_as_float(lo[i + 1])) * inv * w[d + 1];
         const float nb0 = f16_round(__uint_as_float(hi[i])) * inv * w[64 + d];
@@ -156,10 +168,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tm_w);
   }
   float* norm_w = reinterpret_cast<float*>(smem + kNormWOff);
+  int32_t* cu_s = reinterpret_cast<int32_t*>(smem + kCuOff);
+  float* xch = reinterpret_cast<float*>(smem + kXchOff);
+  volatile int* pair_ok = reinterpret_cast<volatile int*>(smem + kPairOkOff);
   if (kQkv) {
     for (int i = threadIdx.x; i < 256; i += kGemmThreads)
       norm_w[i] = i < 128 ? qkv.q_weight[i] : qkv.k_weight[i - 128];
+    if (qkv.batch <= kCuSmem)
+      for (int i = threadIdx.x; i <= qkv.batch; i += kGemmThreads) cu_s[i] = qkv.cu[i];
   }
+  const int32_t* cu_tab = (kQkv && qkv.batch > kCuSmem) ? qkv.cu : cu_s;
   if (warp == 1) {
     tmem_alloc(smem_addr(holder), 512);
     tmem_relinquish();
@@ -231,25 +249,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++lt) {
       const int acc = lt & 1;
       const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * kBN;
-      if (!(ok = mbar_wait(bar(kAccFull + acc), (lt >> 1) & 1, abort_flag, status,
-                           kDevTimeoutAccFull)))
-        break;
-      tc_fence_after();
-      const uint32_t t_cols =
-          tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * kBN + 128 * half;
       const int row = m0 + r;
       const int nt = n0 / kBN;
+      // RoPE table entries of this row, fetched before the accumulator wait
+      float4 tab[16];
+      if (kQkv && nt < 12) {
+        const int pos = row < M ? row - request_start(cu_tab, qkv.batch, row) : 0;
+        const float4* trow =
+            reinterpret_cast<const float4*>(qkv.table + static_cast<int64_t>(pos) * 64) + 16 * half;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) tab[i] = __ldg(trow + i);
+      }
+      ok = mbar_wait(bar(kAccFull + acc), (lt >> 1) & 1, abort_flag, status, kDevTimeoutAccFull);
+      if (kQkv) {
+        // the pair meets at named barriers below: leave the loop together
+        // (each wait above is bounded, so both warps always reach this point)
+        if (lane == 0) pair_ok[sub * 2 + half] = ok ? 1 : 0;
+        pair_sync(sub);
+        ok = pair_ok[sub * 2] && pair_ok[sub * 2 + 1];
+        pair_sync(sub);  // both read before the next tile's write
+      }
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t t_tile = tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * kBN;
+      const uint32_t t_cols = t_tile + 128 * half;
       if (kQkv && nt < 12) {
         // q tiles 0..7 (heads 2nt, 2nt+1), k tiles 8..11 (kv heads 2(nt-8), +1)
         const bool is_q = nt < 8;
-        const bool valid = row < M;
-        const int pos = valid ? row - request_start(qkv.cu, qkv.batch, row) : 0;
-        const float4* trow =
-            reinterpret_cast<const float4*>(qkv.table + static_cast<int64_t>(pos) * 64);
-        const int head = (is_q ? 2 * nt : 2 * (nt - 8)) + half;
-        __half* dst = is_q ? qkv.q_out + (static_cast<int64_t>(row) * 16 + head) * 128
-                           : qkv.k_out + (static_cast<int64_t>(row) * 8 + head) * 128;
-        norm_rope_head(t_cols, norm_w + (is_q ? 0 : 128), trow, qkv.eps, valid, dst);
+        const int head0 = is_q ? 2 * nt : 2 * (nt - 8);
+        __half* dst = is_q ? qkv.q_out + (static_cast<int64_t>(row) * 16 + head0) * 128
+                           : qkv.k_out + (static_cast<int64_t>(row) * 8 + head0) * 128;
+        norm_rope_quarter(t_tile, half, sub, lane, norm_w + (is_q ? 0 : 128), tab, qkv.eps,
+                          row < M, xch, dst);
       } else {
         __half* orow = kQkv ? qkv.v_out + static_cast<int64_t>(row) * 1024 + (n0 - 3072)
                             : out + static_cast<int64_t>(row) * N + n0;
