@@ -14,6 +14,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -429,6 +430,16 @@ qwa_status qwa_qk_norm_rope_padded(qwa_ctx* ctx, const void* qkv, int64_t qkv_st
 
 namespace {
 
+// CTA-pair GEMM for large M (QWA_GEMM_PAIR=0 / 1 forces one shape).
+bool gemm_pair(int m) {
+  static const int forced = [] {
+    const char* e = std::getenv("QWA_GEMM_PAIR");
+    return e ? std::atoi(e) : -1;
+  }();
+  if (forced >= 0) return forced != 0;
+  return m >= kGemmPairMinRows;
+}
+
 qwa_status check_matmul_shape(qwa_ctx* ctx, int m, int n, int k) {
   if (m < 0) return fail(ctx, QWA_ERR_INVALID_ARG, "m must be >= 0");
   if (n < 256 || n % 256 != 0)
@@ -445,11 +456,12 @@ qwa_status run_matmul(qwa_ctx* ctx, const void* input, const void* weight, void*
     return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
   qwa_status st = ensure_encode(ctx);
   if (st != QWA_OK) return st;
+  const bool pair = gemm_pair(m);
   CUtensorMap tm_a, tm_w;
   if ((st = make_map_2d(ctx, &tm_a, input, k, m, 128)) != QWA_OK) return st;
-  if ((st = make_map_2d(ctx, &tm_w, weight, k, n, 256)) != QWA_OK) return st;
+  if ((st = make_map_2d(ctx, &tm_w, weight, k, n, kGemmWBoxRows(pair))) != QWA_OK) return st;
   QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, static_cast<__half*>(output), m, n, k, ctx->d_status,
-                                stream));
+                                pair, stream));
   return QWA_OK;
 }
 
@@ -534,7 +546,8 @@ qwa_status run_qkv_projection(qwa_ctx* ctx, const void* input, const void* weigh
   }
   CUtensorMap tm_a, tm_w;
   if ((st = make_map_2d(ctx, &tm_a, input, k, total, 128)) != QWA_OK) return st;
-  if ((st = make_map_2d(ctx, &tm_w, weight, k, 4096, 256)) != QWA_OK) return st;
+  const bool pair = gemm_pair(total);
+  if ((st = make_map_2d(ctx, &tm_w, weight, k, 4096, kGemmWBoxRows(pair))) != QWA_OK) return st;
   QkvEpilogue e;
   e.q_out = static_cast<__half*>(q_out);
   e.k_out = static_cast<__half*>(k_out);
@@ -545,7 +558,7 @@ qwa_status run_qkv_projection(qwa_ctx* ctx, const void* input, const void* weigh
   e.cu = plan->d_cu;
   e.batch = batch;
   e.eps = eps;
-  QWA_CUDA(ctx, launch_gemm_qkv(tm_a, tm_w, total, k, e, ctx->d_status, s));
+  QWA_CUDA(ctx, launch_gemm_qkv(tm_a, tm_w, total, k, e, ctx->d_status, pair, s));
   return QWA_OK;
 }
 

@@ -6,23 +6,35 @@
 // column n, i.e. output[m, n] = sum_k input[m, k] * W[n, k].
 //
 // Persistent kernel, one CTA per SM, 320 threads:
-//   warp 0      TMA producer: A tile 128 x 64 and W tile 256 x 64 per stage
-//               (128-byte swizzle), 4-stage ring;
-//   warp 1      TMEM owner and single MMA issuer: per stage 4 x
-//               tcgen05.mma M=128 N=256 K=16 into one of two accumulators;
+//   warp 0      TMA producer (per stage an A tile of 128 rows x 64 and a W
+//               tile, 128-byte swizzle);
+//   warp 1      TMEM owner and single MMA issuer (tcgen05.mma K=16 steps
+//               into one of two 256-column accumulators);
 //   warps 2..9  epilogue: tcgen05.ld of the accumulator (thread = row; the
 //               two warps of a TMEM sub-partition take one 128-column half
 //               each), f32 -> f16, 16-byte stores; releases the accumulator
 //               so the MMAs of the next tile overlap this tile's stores.
+// Two shapes of the same kernel:
+//   single CTA  (kPair = false): 128 x 256 tiles, W tile 256 x 64, 4 stages
+//               of 48 KB, tcgen05.mma.cta_group::1 M=128 N=256;
+//   CTA pair    (kPair = true, clusters of 2): 256 x 256 tiles; each CTA
+//               loads its own 128 rows of A and its 128-row half of the W
+//               tile (32 KB per stage, 6 stages), both CTAs' loads complete
+//               on the even CTA's barrier, and the even CTA alone issues
+//               tcgen05.mma.cta_group::2 M=256 N=256, which reads the odd
+//               CTA's operands at the same shared-memory offsets and
+//               accumulates rows 128..255 in the odd CTA's TMEM. Per FLOP
+//               this halves the W traffic and cuts the shared-memory operand
+//               feed by a third. No load is multicast.
 // With the QKV epilogue (N = 4096, the attn_qkv projection of
 // src/webgpu/model.ts:93), a 256-column tile holds two whole heads of each
-// row, so the epilogue thread of a row also applies the per-head Q/K RMSNorm
-// + RoPE of qkNormRopeShader (src/webgpu/ops.ts:104-150) to the q and k
-// tiles and writes q [T,16,128], k [T,8,128] and v [T,8,128] directly: the
-// [T, 4096] qkvRaw round trip and the separate prologue launch disappear.
-// The arithmetic is the unfused pipeline's, step for step (accumulator
-// rounded to f16 as qkvRaw would be, the prologue kernel's f32 sum order,
-// normalisation and rotation), so both paths give identical bits.
+// row, so the epilogue also applies the per-head Q/K RMSNorm + RoPE of
+// qkNormRopeShader (src/webgpu/ops.ts:104-150) to the q and k tiles and
+// writes q [T,16,128], k [T,8,128] and v [T,1024] directly: the [T, 4096]
+// qkvRaw round trip and the separate prologue launch disappear. The
+// arithmetic is the unfused pipeline's, step for step (accumulator rounded to
+// f16 as qkvRaw would be, the prologue kernel's f32 sum order, normalisation
+// and rotation), so both paths give identical bits.
 // Output tiles are walked n-fastest so consecutive tiles of a CTA (and the
 // CTAs running at the same time) share the A rows in L2; W (<= 12 MB for
 // Qwen3-0.6B) stays L2-resident.
@@ -32,27 +44,35 @@
 namespace qwa {
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
+constexpr int kBK = 64, kBN = 256;
 constexpr int kCuSmem = 1024;  // requests whose cu_seqlens are staged in shared memory
 constexpr int kGemmThreads = 320;
-constexpr int kEpiThreads = 256;
-constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;  // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kBarOff = kStages * kStageBytes;  // 192 KB
-// barriers: full[4], empty[4], acc_full[2], acc_empty[2]
-constexpr int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages, kAccEmpty = 2 * kStages + 2;
-constexpr int kNumBars = 2 * kStages + 4;
-constexpr uint32_t kNormWOff = kBarOff + 8 * kNumBars;  // q / k norm weights, 2 x 128 f32
-constexpr uint32_t kCuOff = kNormWOff + 2 * 128 * 4;       // cu_seqlens, kCuSmem + 1 ints
-constexpr uint32_t kXchOff = kCuOff + (kCuSmem + 4) * 4;    // norm partial sums, 8 KB
-constexpr uint32_t kPairOkOff = kXchOff + 4 * 2 * 2 * 128 * 4;  // 8 ints
-constexpr uint32_t kHolderOff = kPairOkOff + 8 * 4;
-constexpr uint32_t kAbortOff = kHolderOff + 4;
-constexpr uint32_t kGemmSmem = kAbortOff + 4 + 1024;  // + alignment slack
-static_assert(kGemmSmem <= 232448, "shared memory budget");
-constexpr uint32_t kIdesc = idesc_f16_f32(kBM, kBN, false);
+constexpr int kEpiWarps = 8;
+
+// Shared-memory layout of one shape.
+template <bool kPair>
+struct Layout {
+  static constexpr int kStages = kPair ? 6 : 4;
+  static constexpr uint32_t kABytes = 128 * kBK * 2;                      // 16 KB
+  static constexpr uint32_t kBBytes = (kPair ? 128 : 256) * kBK * 2;      // 16 / 32 KB
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarOff = kStages * kStageBytes;              // 192 KB
+  // barriers: full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages,
+                       kAccEmpty = 2 * kStages + 2, kNumBars = 2 * kStages + 4;
+  static constexpr uint32_t kNormWOff = kBarOff + 8 * kNumBars;     // 2 x 128 f32
+  static constexpr uint32_t kCuOff = kNormWOff + 2 * 128 * 4;       // kCuSmem + 1 ints
+  static constexpr uint32_t kXchOff = kCuOff + (kCuSmem + 4) * 4;   // 8 KB of partial sums
+  static constexpr uint32_t kPairOkOff = kXchOff + 4 * 2 * 2 * 128 * 4;
+  static constexpr uint32_t kHolderOff = kPairOkOff + 8 * 4;
+  static constexpr uint32_t kAbortOff = kHolderOff + 4;
+  static constexpr uint32_t kSmem = kAbortOff + 4 + 1024;  // + alignment slack
+  static_assert(kSmem <= 232448, "shared memory budget");
+  static constexpr uint32_t kIdesc = idesc_f16_f32(kPair ? 256 : 128, kBN, false);
+  static constexpr int kRowsPerTile = kPair ? 256 : 128;
+  // arrivals that free an accumulator: one per epilogue warp of each CTA
+  static constexpr uint32_t kAccEmptyCount = kPair ? 2 * kEpiWarps : kEpiWarps;
+};
 
 // Start row of the request holding row t: binary search over cu[0..batch].
 __device__ __forceinline__ int request_start(const int32_t* cu, int batch, int t) {
@@ -139,38 +159,44 @@ __device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int su
   }
 }
 
-template <bool kQkv>
+template <bool kQkv, bool kPair>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_w, __half* __restrict__ out, int M,
                     int N, int K, int* status, const QkvEpilogue qkv) {
+  using L = Layout<kPair>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t sbase = smem_addr(smem);
-  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + kHolderOff);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
-  auto bar = [&](int i) -> uint32_t { return sbase + kBarOff + 8u * i; };
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + L::kHolderOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kAbortOff);
+  auto bar = [&](int i) -> uint32_t { return sbase + L::kBarOff + 8u * i; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // CTA pair: rank 0 (even) is the leader that issues the MMAs
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kFull + s), 1);
-      mbar_init(bar(kEmpty + s), 1);
+    for (int s = 0; s < L::kStages; ++s) {
+      mbar_init(bar(L::kFull + s), 1);
+      mbar_init(bar(L::kEmpty + s), 1);
     }
     for (int a = 0; a < 2; ++a) {
-      mbar_init(bar(kAccFull + a), 1);
-      mbar_init(bar(kAccEmpty + a), kEpiThreads);
+      mbar_init(bar(L::kAccFull + a), 1);
+      mbar_init(bar(L::kAccEmpty + a), L::kAccEmptyCount);
     }
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_w);
   }
-  float* norm_w = reinterpret_cast<float*>(smem + kNormWOff);
-  int32_t* cu_s = reinterpret_cast<int32_t*>(smem + kCuOff);
-  float* xch = reinterpret_cast<float*>(smem + kXchOff);
-  volatile int* pair_ok = reinterpret_cast<volatile int*>(smem + kPairOkOff);
+  float* norm_w = reinterpret_cast<float*>(smem + L::kNormWOff);
+  int32_t* cu_s = reinterpret_cast<int32_t*>(smem + L::kCuOff);
+  float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
+  volatile int* pair_ok = reinterpret_cast<volatile int*>(smem + L::kPairOkOff);
   if (kQkv) {
     for (int i = threadIdx.x; i < 256; i += kGemmThreads)
       norm_w[i] = i < 128 ? qkv.q_weight[i] : qkv.k_weight[i - 128];
@@ -179,76 +205,104 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   const int32_t* cu_tab = (kQkv && qkv.batch > kCuSmem) ? qkv.cu : cu_s;
   if (warp == 1) {
-    tmem_alloc(smem_addr(holder), 512);
-    tmem_relinquish();
+    if (kPair) {
+      tmem_alloc_pair(smem_addr(holder), 512);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_addr(holder), 512);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (kPair) cluster_sync();  // barriers and TMEM of both CTAs are ready
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *holder;
 
   const int tiles_n = N / kBN;
-  const int num_tiles = ((M + kBM - 1) / kBM) * tiles_n;
+  const int num_tiles = ((M + L::kRowsPerTile - 1) / L::kRowsPerTile) * tiles_n;
   const int kblocks = K / kBK;
 
   if (warp == 0) {
+    // ---------------------------------------------------------- producer
     if (lane == 0) {
       bool ok = true;
       int c = 0;  // stage uses
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * kBN;
+      const uint32_t full0 = kPair ? mapa_shared(bar(L::kFull), 0) : bar(L::kFull);
+      for (int tile = unit; ok && tile < num_tiles; tile += units) {
+        const int m0 = (tile / tiles_n) * L::kRowsPerTile + static_cast<int>(rank) * 128;
+        const int n0 = (tile % tiles_n) * kBN + (kPair ? static_cast<int>(rank) * 128 : 0);
         for (int kb = 0; kb < kblocks; ++kb, ++c) {
-          const int s = c % kStages;
-          if (!(ok = mbar_wait(bar(kEmpty + s), ((c / kStages) & 1) ^ 1, abort_flag, status,
+          const int s = c % L::kStages;
+          if (!(ok = mbar_wait(bar(L::kEmpty + s), ((c / L::kStages) & 1) ^ 1, abort_flag, status,
                                kDevTimeoutGemmEmpty)))
             break;
-          const uint32_t dst = sbase + s * kStageBytes;
-          mbar_arrive_expect_tx(bar(kFull + s), kStageBytes);
-          tma_load_2d(dst, &tm_a, bar(kFull + s), kb * kBK, m0);
-          tma_load_2d(dst + kABytes, &tm_w, bar(kFull + s), kb * kBK, n0);
+          const uint32_t dst = sbase + s * L::kStageBytes;
+          if (kPair) {
+            // the leader's full barrier counts both CTAs' bytes
+            if (leader) mbar_arrive_expect_tx(bar(L::kFull + s), 2 * L::kStageBytes);
+            tma_load_2d_pair(dst, &tm_a, full0 + 8u * s, kb * kBK, m0);
+            tma_load_2d_pair(dst + L::kABytes, &tm_w, full0 + 8u * s, kb * kBK, n0);
+          } else {
+            mbar_arrive_expect_tx(bar(L::kFull + s), L::kStageBytes);
+            tma_load_2d(dst, &tm_a, bar(L::kFull + s), kb * kBK, m0);
+            tma_load_2d(dst + L::kABytes, &tm_w, bar(L::kFull + s), kb * kBK, n0);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0 && leader) {
       bool ok = true;
       int c = 0, lt = 0;  // stage uses, local tiles
       const uint64_t a_desc0 = smem_desc_sw128(sbase, 16, 1024);
-      const uint64_t b_desc0 = smem_desc_sw128(sbase + kABytes, 16, 1024);
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++lt) {
+      const uint64_t b_desc0 = smem_desc_sw128(sbase + L::kABytes, 16, 1024);
+      for (int tile = unit; ok && tile < num_tiles; tile += units, ++lt) {
         const int acc = lt & 1;
-        if (!(ok = mbar_wait(bar(kAccEmpty + acc), ((lt >> 1) & 1) ^ 1, abort_flag, status,
+        if (!(ok = mbar_wait(bar(L::kAccEmpty + acc), ((lt >> 1) & 1) ^ 1, abort_flag, status,
                              kDevTimeoutAccEmpty)))
           break;
         tc_fence_after();
         const uint32_t d = tmem + acc * kBN;
         for (int kb = 0; kb < kblocks; ++kb, ++c) {
-          const int s = c % kStages;
-          if (!(ok = mbar_wait(bar(kFull + s), (c / kStages) & 1, abort_flag, status,
+          const int s = c % L::kStages;
+          if (!(ok = mbar_wait(bar(L::kFull + s), (c / L::kStages) & 1, abort_flag, status,
                                kDevTimeoutGemmFull)))
             break;
           tc_fence_after();
-          const uint64_t so = (s * kStageBytes) >> 4;
+          const uint64_t so = (s * L::kStageBytes) >> 4;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_ss(d, a_desc0 + so + ((kk * 32) >> 4), b_desc0 + so + ((kk * 32) >> 4), kIdesc,
-                   (kb > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(bar(kEmpty + s));
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ko = so + ((kk * 32) >> 4);
+            if (kPair)
+              mma_ss_pair(d, a_desc0 + ko, b_desc0 + ko, L::kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            else
+              mma_ss(d, a_desc0 + ko, b_desc0 + ko, L::kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (kPair) tc_commit_pair(bar(L::kEmpty + s), 0x3);
+          else tc_commit(bar(L::kEmpty + s));
         }
-        if (ok) tc_commit(bar(kAccFull + acc));
+        if (ok) {
+          if (kPair) tc_commit_pair(bar(L::kAccFull + acc), 0x3);
+          else tc_commit(bar(L::kAccFull + acc));
+        }
       }
     }
   } else {
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its sub-partition);
-    // warps 2..5 take columns 0..127 of the tile, warps 6..9 columns 128..255
+    // --------------------------------------------------------- epilogue
+    // warp w reads TMEM lanes 32*(w%4) .. +31 (its sub-partition); warps
+    // 2..5 take columns 0..127 of the tile, warps 6..9 columns 128..255
     const int sub = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = sub * 32 + lane;
+    const uint32_t acc_empty0 = kPair ? mapa_shared(bar(L::kAccEmpty), 0) : bar(L::kAccEmpty);
     bool ok = true;
     int lt = 0;
-    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++lt) {
+    for (int tile = unit; ok && tile < num_tiles; tile += units, ++lt) {
       const int acc = lt & 1;
-      const int m0 = (tile / tiles_n) * kBM, n0 = (tile % tiles_n) * kBN;
+      const int m0 = (tile / tiles_n) * L::kRowsPerTile + static_cast<int>(rank) * 128;
+      const int n0 = (tile % tiles_n) * kBN;
       const int row = m0 + r;
       const int nt = n0 / kBN;
       // RoPE table entries of this row, fetched before the accumulator wait
@@ -260,7 +314,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) tab[i] = __ldg(trow + i);
       }
-      ok = mbar_wait(bar(kAccFull + acc), (lt >> 1) & 1, abort_flag, status, kDevTimeoutAccFull);
+      ok = mbar_wait(bar(L::kAccFull + acc), (lt >> 1) & 1, abort_flag, status, kDevTimeoutAccFull);
       if (kQkv) {
         // the pair meets at named barriers below: leave the loop together
         // (each wait above is bounded, so both warps always reach this point)
@@ -304,22 +358,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      // this warp's reads of the accumulator are complete (wait::ld above)
       tc_fence_before();
-      mbar_arrive(bar(kAccEmpty + acc));
+      __syncwarp();
+      if (lane == 0) {
+        if (kPair) mbar_arrive_cluster(acc_empty0 + 8u * acc);
+        else mbar_arrive(bar(L::kAccEmpty + acc));
+      }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
+  if (kPair) cluster_sync();  // no CTA leaves while its peer may still signal it
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    if (kPair) tmem_dealloc_pair(tmem, 512);
+    else tmem_dealloc(tmem, 512);
   }
 }
 
-template <bool kQkv>
+template <bool kQkv, bool kPair>
 cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
                         int N, int K, int* status, const QkvEpilogue& qkv, cudaStream_t stream) {
+  using L = Layout<kPair>;
   static bool configured[kMaxDevices] = {};
   static int sm_count[kMaxDevices] = {};
   int dev = 0;
@@ -327,32 +389,51 @@ cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_f16_kernel<kQkv>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kGemmSmem);
+    e = cudaFuncSetAttribute(gemm_f16_kernel<kQkv, kPair>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem);
     if (e == cudaSuccess)
       e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  const int sms = sm_count[dev];
-  const int tiles = ((M + kBM - 1) / kBM) * (N / kBN);
-  const int grid = tiles < sms ? tiles : sms;
-  if (grid <= 0) return cudaSuccess;
-  gemm_f16_kernel<kQkv><<<grid, kGemmThreads, kGemmSmem, stream>>>(tm_a, tm_w, out, M, N, K,
-                                                                   status, qkv);
+  const int tiles = ((M + L::kRowsPerTile - 1) / L::kRowsPerTile) * (N / kBN);
+  if (tiles <= 0) return cudaSuccess;
+  if (kPair) {
+    const int pairs = sm_count[dev] / 2;
+    const int grid = 2 * (tiles < pairs ? tiles : pairs);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = L::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair>, tm_a, tm_w, out, M, N, K,
+                              status, qkv);
+  }
+  const int grid = tiles < sm_count[dev] ? tiles : sm_count[dev];
+  gemm_f16_kernel<kQkv, kPair><<<grid, kGemmThreads, L::kSmem, stream>>>(tm_a, tm_w, out, M, N,
+                                                                          K, status, qkv);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
-                            int N, int K, int* status, cudaStream_t stream) {
-  return launch_gemm<false>(tm_a, tm_w, out, M, N, K, status, QkvEpilogue{}, stream);
+                            int N, int K, int* status, bool pair, cudaStream_t stream) {
+  return pair ? launch_gemm<false, true>(tm_a, tm_w, out, M, N, K, status, QkvEpilogue{}, stream)
+              : launch_gemm<false, false>(tm_a, tm_w, out, M, N, K, status, QkvEpilogue{}, stream);
 }
 
 cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
-                            const QkvEpilogue& qkv, int* status, cudaStream_t stream) {
-  return launch_gemm<true>(tm_a, tm_w, nullptr, M, 4096, K, status, qkv, stream);
+                            const QkvEpilogue& qkv, int* status, bool pair, cudaStream_t stream) {
+  return pair ? launch_gemm<true, true>(tm_a, tm_w, nullptr, M, 4096, K, status, qkv, stream)
+              : launch_gemm<true, false>(tm_a, tm_w, nullptr, M, 4096, K, status, qkv, stream);
 }
 
 }  // namespace qwa

@@ -110,10 +110,13 @@ cudaError_t launch_last_token_pool(const __half* hidden, int width, const int32_
 constexpr int kMaxDevices = 64;
 
 // C[M,N] = A[M,K] W[N,K]^T, f16 in/out, f32 accumulate (tcgen05). tm_a: 2-D
-// map {K, M} box {64, 128}; tm_w: {K, N} box {64, 256}; 128-byte swizzle.
-// N % 256 == 0, K % 64 == 0.
+// map {K, M} box {64, 128}; tm_w: {K, N} box {64, kGemmWBoxRows(pair)};
+// 128-byte swizzle. N % 256 == 0, K % 64 == 0. pair: 256-row tiles on CTA
+// pairs (cta_group::2), for large M.
+constexpr int kGemmWBoxRows(bool pair) { return pair ? 128 : 256; }
+constexpr int kGemmPairMinRows = 4096;
 cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
-                            int N, int K, int* status, cudaStream_t stream);
+                            int N, int K, int* status, bool pair, cudaStream_t stream);
 
 // Fused attn_qkv projection epilogue: per-head Q/K RMSNorm + RoPE on the q/k
 // tiles, v written as [T, 1024]. Positions are row - cu[request(row)].
@@ -131,7 +134,7 @@ struct QkvEpilogue {
 
 // QKV projection (N = 4096) with the QkvEpilogue; K % 64 == 0.
 cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
-                            const QkvEpilogue& qkv, int* status, cudaStream_t stream);
+                            const QkvEpilogue& qkv, int* status, bool pair, cudaStream_t stream);
 
 // Q4_0 tile32-compact records (20 bytes: f16 scale, 2 pad bytes, 16 bytes of
 // nibbles) -> f16 W[n, k] row-major.

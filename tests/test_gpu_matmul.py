@@ -45,6 +45,7 @@ def test_dequant_bit_exact(pkg, cuda_dev, n, k):
 @pytest.mark.parametrize("m,n,k", [
     (1, 256, 64), (50, 1024, 1024), (128, 4096, 1024), (1000, 1024, 2048),
     (777, 512, 3072), (5000, 4096, 1024), (300, 6144, 1024),
+    (4096, 256, 64), (9000, 1024, 2048),  # M >= 4096 runs on CTA pairs (cta_group::2)
 ])
 def test_matmul_matches_oracle(pkg, cuda_dev, m, n, k):
     mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
