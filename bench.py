@@ -48,6 +48,11 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--gemm", action="store_true",
+                    help="time the projection GEMM against cuBLAS and the fused QKV projection")
+    ap.add_argument("--gemm-rows", type=int, default=0,
+                    help="with --gemm: one M (rows) instead of the default shapes; small runs "
+                         "for profiling")
     ap.add_argument("--engine", action="store_true",
                     help="time the micro-batch engine, padded vs varlen packing (one GPU)")
     # profiling aids: shrink the workload (never used for the reported line)
@@ -321,8 +326,85 @@ def run_engine(args):
     print(json.dumps(line), flush=True)
 
 
+def _graph_ms(torch, fn, reps=10):
+    """Mean ms of fn over a CUDA graph of `reps` calls (events on its stream)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(reps):
+            fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def run_gemm(args):
+    """Projection GEMM (tcgen05) against cuBLAS on the engine's shapes, and the
+    fused attn_qkv projection + Q/K norm + RoPE against GEMM + prologue. Inputs
+    are larger than L2 except where stated; each number is a CUDA graph of 10
+    launches timed with events."""
+    import torch
+    pkg = importlib.import_module(PKG)
+    mm, attn = pkg.matmul, pkg.attention
+    torch.cuda.set_device(0)
+    peaks, psrc = measured_peaks()
+    lengths = pkg.workloads.ragged_lengths(16, 15, 5000, 2025)  # the engine's micro-batch
+    T = int(sum(lengths))
+    shapes = ([(args.gemm_rows, 4096, 1024)] if args.gemm_rows else
+              [(T, 4096, 1024), (T, 1024, 2048), (80000, 4096, 1024), (8192, 4096, 1024),
+               (16384, 16384, 1024)])
+    lines = []
+    with ClockSampler(0) as clocks:
+        for m, n, k in shapes:
+            a = torch.randn(m, k, device="cuda").half()
+            w = (torch.randn(n, k, device="cuda") * k ** -0.5).half()
+            out = torch.empty(m, n, device="cuda", dtype=torch.float16)
+            ours = _graph_ms(torch, lambda: mm.matmul(a, w, out))
+            cub = _graph_ms(torch, lambda: torch.matmul(a, w.t(), out=out))
+            flop = 2.0 * m * n * k
+            lines.append({"shape": [m, n, k], "ours_ms": ours, "ours_tflops": flop / ours / 1e9,
+                          "cublas_ms": cub, "cublas_tflops": flop / cub / 1e9,
+                          "cta_pairs": m >= 4096})
+        rows = args.gemm_rows or T
+        cu = [0] + list(np.cumsum(lengths if not args.gemm_rows else [rows]).astype(int).tolist())
+        x = torch.randn(rows, 1024, device="cuda").half()
+        w = (torch.randn(4096, 1024, device="cuda") * 1024 ** -0.5).half()
+        qw = torch.ones(128, device="cuda")
+        kw = torch.ones(128, device="cuda")
+        q = torch.empty(rows, 16, 128, device="cuda", dtype=torch.half)
+        kk = torch.empty(rows, 8, 128, device="cuda", dtype=torch.half)
+        v = torch.empty(rows, 1024, device="cuda", dtype=torch.half)
+        qkv = torch.empty(rows, 4096, device="cuda", dtype=torch.half)
+        fused = _graph_ms(torch, lambda: mm.qkv_projection(x, w, qw, kw, cu, q_out=q, k_out=kk,
+                                                          v_out=v))
+        gemm = _graph_ms(torch, lambda: mm.matmul(x, w, qkv))
+        pro = _graph_ms(torch, lambda: attn.qk_norm_rope(qkv, qw, kw, cu, q_out=q, k_out=kk))
+    line = {
+        "metric": "projection GEMM TFLOP/s (f16 in, f32 accumulate)", "unit": "TFLOP/s",
+        "value": lines[0]["ours_tflops"], "n_gpus": 1, "dtype": "f16",
+        "peak_tflops": peaks["bf16_tflops"], "peak_source": f"{psrc} bf16_tflops (burst)",
+        "shapes": lines,
+        "qkv_projection": {"rows": rows, "fused_ms": fused, "gemm_ms": gemm, "prologue_ms": pro,
+                           "unfused_ms": gemm + pro, "speedup": (gemm + pro) / fused},
+        "timing": "CUDA graph of 10 launches per number, events", "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.gemm:
+        run_gemm(args)
+        return
     if args.engine:
         run_engine(args)
         return
