@@ -202,7 +202,7 @@ class AttentionStackRuntime:
     """
 
     def __init__(self, layers: int = 28, vocab: int = 151669, hidden: int = 1024,
-                 device: Optional[int] = None, seed: int = 0):
+                 device: Optional[int] = None, seed: int = 0, weights=None):
         from . import attention as attn
         from . import matmul, norm, prepacked
         self._attn = attn
@@ -234,6 +234,24 @@ class AttentionStackRuntime:
         self.k_norm = [gains(128) for _ in range(layers)]
         self.in_norm = [gains(hidden) for _ in range(layers)]
         self.final_norm = gains(hidden)
+        if weights is not None:
+            self._use_prepacked(weights)
+
+    def _use_prepacked(self, weights) -> None:
+        """Take the attention-half tensors of a PrepackedWeights
+        (blk.N.attn_qkv / attn_output compact Q4_0, attn_q_norm, attn_k_norm,
+        attn_norm, output_norm). The token embedding stays seeded: the
+        reference stores it as Q6_K, whose lookup is not part of this path."""
+        n = weights.layers()
+        if n < self.layers:
+            raise ValueError(f"prepacked weights hold {n} layers; runtime needs {self.layers}")
+        for l in range(self.layers):
+            t = weights.attention_layer(l)
+            self.w_qkv[l], self.w_o[l] = t["attn_qkv"], t["attn_output"]
+            self.q_norm[l], self.k_norm[l] = t["attn_q_norm"].float(), t["attn_k_norm"].float()
+            self.in_norm[l] = t["attn_norm"].float()
+        if "output_norm.weight" in weights.tensors:
+            self.final_norm = weights.weight("output_norm.weight").float()
 
     def _project(self, x: torch.Tensor, w: torch.Tensor, n: int) -> torch.Tensor:
         m, k = x.shape

@@ -175,3 +175,69 @@ def q40_part(name: str, rows: np.ndarray, k: int) -> Q40TensorPart:
 
 def dimensions_kn(t: PackedTensorBytes) -> Tuple[int, int]:
     return t.dimensions[0], t.dimensions[1]
+
+
+# ------------------------------------------------------------------ device load
+
+ATTENTION_TENSORS = ("attn_norm", "attn_qkv", "attn_q_norm", "attn_k_norm", "attn_output")
+
+
+class PrepackedWeights:
+    """Tensors of a parsed .wgpack uploaded to one CUDA device, as the
+    reference's Qwen3WebGPUModel does for a prepacked source
+    (src/webgpu/model.ts:209-224): compact Q4_0 matrices stay packed (uint8;
+    the matmul path dequantises each once), raw F32 / F16 tensors become
+    float32 / float16 tensors, other raw types (the Q6_K token embedding) are
+    kept as bytes. ``dims[name]`` is the reference's [k, n] / shape list."""
+
+    def __init__(self, model: PrepackedModel, device=None):
+        import torch
+        self.device = torch.device("cuda", torch.cuda.current_device() if device is None
+                                   else device)
+        self.tensors: Dict[str, "torch.Tensor"] = {}
+        self.dims: Dict[str, List[int]] = {}
+        self.storage: Dict[str, str] = {}
+        self.metadata = model.header.get("metadata", {})
+        for name, t in model.tensors.items():
+            raw = model.tensor_bytes(name)
+            if t["storage"] == STORAGE_RAW and t["type"] == GGML_F32:
+                host = np.frombuffer(raw.tobytes(), np.float32)
+            elif t["storage"] == STORAGE_RAW and t["type"] == GGML_F16:
+                host = np.frombuffer(raw.tobytes(), np.float16)
+            else:
+                host = np.array(raw, dtype=np.uint8)
+            self.tensors[name] = torch.from_numpy(np.array(host)).to(self.device)
+            self.dims[name] = list(t["dimensions"])
+            self.storage[name] = t["storage"]
+
+    @classmethod
+    def from_file(cls, path: str, device=None) -> "PrepackedWeights":
+        with open(path, "rb") as f:
+            return cls(parse_prepacked_model(f.read()), device)
+
+    def weight(self, name: str):
+        """Model.weight (model.ts:250-254): the tensor, or an error naming it."""
+        t = self.tensors.get(name)
+        if t is None:
+            raise KeyError(f"missing tensor {name}")
+        return t
+
+    def layers(self) -> int:
+        n = 0
+        while f"blk.{n}.attn_qkv.weight" in self.tensors:
+            n += 1
+        return n
+
+    def attention_layer(self, layer: int) -> Dict[str, "torch.Tensor"]:
+        """The attention-half tensors of one block, by the reference's names
+        (model.ts:89-100): attn_norm, attn_qkv (compact [1024, 4096]),
+        attn_q_norm, attn_k_norm, attn_output (compact [2048, 1024])."""
+        out = {}
+        for key in ATTENTION_TENSORS:
+            name = f"blk.{layer}.{key}.weight"
+            out[key] = self.weight(name)
+        for key, kn in (("attn_qkv", [1024, 4096]), ("attn_output", [2048, 1024])):
+            name = f"blk.{layer}.{key}.weight"
+            if self.storage[name] != STORAGE_COMPACT or self.dims[name] != kn:
+                raise ValueError(f"{name} must be a compact Q4_0 matrix of dimensions {kn}")
+        return out

@@ -83,3 +83,57 @@ def test_engine_varlen_equals_padded_and_single(pkg, cuda_dev):
     for other in (pad, single):
         cos = np.sum(var * other, axis=1)
         assert cos.min() >= 0.9999, cos
+
+
+def test_engine_runtime_from_prepacked_file(pkg, cuda_dev, tmp_path):
+    """A synthetic .wgpack with the reference's tensor names loads onto the
+    device, and the runtime built from it embeds like the seeded one built from
+    the same packed bytes."""
+    import asyncio
+    pp = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.prepacked")
+    eng_mod = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.engine")
+    rng = np.random.default_rng(4)
+    layers, tensors = 2, []
+    for l in range(layers):
+        tensors.append(pp.pack_q40_tile32(f"blk.{l}.attn_qkv.weight", [
+            pp.q40_part("q", pp.random_q40_rows(rng, 2048, 1024, 0.006), 1024),
+            pp.q40_part("k", pp.random_q40_rows(rng, 1024, 1024, 0.006), 1024),
+            pp.q40_part("v", pp.random_q40_rows(rng, 1024, 1024, 0.006), 1024)]))
+        tensors.append(pp.pack_q40_tile32(f"blk.{l}.attn_output.weight", [
+            pp.q40_part("o", pp.random_q40_rows(rng, 1024, 2048, 0.004), 2048)]))
+        for key, n in (("attn_q_norm", 128), ("attn_k_norm", 128), ("attn_norm", 1024)):
+            tensors.append(pp.raw_tensor(f"blk.{l}.{key}.weight", [n], pp.GGML_F32,
+                                         (1 + 0.02 * rng.standard_normal(n)).astype(np.float32)))
+    tensors.append(pp.raw_tensor("output_norm.weight", [1024], pp.GGML_F32,
+                                 np.ones(1024, np.float32)))
+    path = tmp_path / "tiny.wgpack"
+    path.write_bytes(pp.build_prepacked_file("0" * 64, 0, {"general.name": "tiny"}, tensors))
+    weights = pp.PrepackedWeights.from_file(str(path), 0)
+    assert weights.layers() == 2 and weights.metadata["general.name"] == "tiny"
+    assert weights.weight("blk.1.attn_qkv.weight").dtype == torch.uint8
+    assert weights.weight("blk.0.attn_q_norm.weight").dtype == torch.float32
+    with pytest.raises(KeyError, match="missing tensor"):
+        weights.weight("blk.9.attn_qkv.weight")
+    rt = eng_mod.AttentionStackRuntime(layers=2, vocab=4096, seed=3, weights=weights)
+    reqs = _requests(np.random.default_rng(1), [40, 300, 7], 4096)
+
+    async def run():
+        eng = eng_mod.EmbeddingEngine(rt, None, 16, 0, 4095, packing="varlen")
+        return await asyncio.gather(*[eng.submit_tokens(r) for r in reqs])
+
+    emb = np.stack(asyncio.run(run()))
+    assert np.isfinite(emb).all() and np.allclose(np.linalg.norm(emb, axis=1), 1, atol=1e-5)
+    # the same layers through matmul + attention, step by step, match
+    mm, attn, norm = pkg.matmul, pkg.attention, pkg.norm
+    cu = [0, 40, 340, 347]
+    ids = torch.from_numpy(np.concatenate(reqs).astype(np.int64)).cuda()
+    x = rt.embed_table[ids]
+    h = norm.rms_norm(x, rt.in_norm[0])
+    for l in range(2):
+        qkv = mm.matmul(h, mm.q40_dequantize(rt.w_qkv[l], 4096, 1024))
+        o = attn.prefill_attention_layer(qkv, rt.q_norm[l], rt.k_norm[l], cu)
+        delta = mm.matmul(o.view(-1, 2048), mm.q40_dequantize(rt.w_o[l], 1024, 2048))
+        nxt = rt.in_norm[l + 1] if l + 1 < 2 else rt.final_norm
+        norm.rms_norm(x, nxt, residual=delta, out=h)
+    ref = pkg.pooling.last_token_pool(h, cu).cpu().numpy()
+    assert np.array_equal(ref, emb)
