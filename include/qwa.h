@@ -216,8 +216,10 @@ QWA_API qwa_status qwa_q40_dequantize(qwa_ctx *ctx, const void *packed, int n, i
  * encode for the prepacked tile32 layout (quant-matmul.ts:495-540): the
  * first call for a given (packed, n, k) dequantises the matrix into an f16
  * copy owned by the context (n * k * 2 bytes, kept until qwa_q40_forget or
- * qwa_destroy); every call then runs qwa_matmul on that copy. A caller that
- * rewrites the packed buffer in place calls qwa_q40_forget first. */
+ * qwa_destroy); every call then runs qwa_matmul on that copy. The copy is
+ * found by the packed buffer's address: a caller that rewrites the packed
+ * buffer in place, or frees it (the address may later hold another matrix),
+ * calls qwa_q40_forget first. */
 QWA_API qwa_status qwa_q40_matmul(qwa_ctx *ctx, const void *input, const void *packed,
                                   void *output, int m, int n, int k, void *stream);
 

@@ -12,6 +12,7 @@ f32 accumulation (csrc/gemm.cu); the reference accumulates in f16.
 from __future__ import annotations
 
 import ctypes
+import weakref
 from dataclasses import dataclass
 from typing import Optional
 
@@ -26,6 +27,26 @@ LAYOUT_TILE32 = "q4_0-tile32-compact"
 def packed_bytes(n: int, k: int) -> int:
     """Size of a tile32-compact matrix: ceil(n/32) * (k/32) * 32 records of 20 B."""
     return (n + 31) // 32 * (k // 32) * 32 * 20
+
+
+_tracked: dict = {}  # (device, data_ptr) of packed tensors with a forget finalizer
+
+
+def _track_packed(ctx: Context, packed: torch.Tensor) -> None:
+    """The context caches an f16 copy of a packed matrix keyed by its device
+    address; drop it when the tensor dies, before the allocator can hand the
+    same address to another buffer."""
+    key = (ctx.device, packed.data_ptr())
+    if key in _tracked:
+        return
+    lib, handle, ptr = ctx.lib, ctx.handle, packed.data_ptr()
+
+    def forget():
+        _tracked.pop(key, None)
+        if ctx.handle:
+            lib.qwa_q40_forget(handle, ctypes.c_void_p(ptr))
+
+    _tracked[key] = weakref.finalize(packed, forget)
 
 
 def _f16(t: torch.Tensor, name: str, numel: int) -> None:
@@ -67,6 +88,7 @@ class QuantMatmulKernel:
         return QuantMatmulRun(input, weights, output, m, n, k)
 
     def encode(self, stream, run: QuantMatmulRun) -> None:
+        _track_packed(self.ctx, run.weights)
         st = self.ctx.lib.qwa_q40_matmul(self.ctx.handle, _ptr(run.input), _ptr(run.weights),
                                          _ptr(run.output), run.m, run.n, run.k, _stream(stream))
         _lib.check(st, self.ctx.handle)
@@ -74,6 +96,9 @@ class QuantMatmulKernel:
     def forget(self, weights: torch.Tensor) -> None:
         """Drop the f16 copy made from ``weights`` (after rewriting it in place)."""
         _lib.check(self.ctx.lib.qwa_q40_forget(self.ctx.handle, _ptr(weights)), self.ctx.handle)
+        f = _tracked.pop((self.ctx.device, weights.data_ptr()), None)
+        if f is not None:
+            f.detach()
 
 
 def q40_dequantize(packed: torch.Tensor, n: int, k: int, out: Optional[torch.Tensor] = None,
@@ -131,6 +156,7 @@ def qkv_projection(input: torch.Tensor, weight: torch.Tensor, q_weight: torch.Te
         _need(weight.is_cuda and weight.numel() >= packed_bytes(4096, k),
               "packed weight must be a CUDA tile32-compact buffer of [4096, k]")
         fn = ctx.lib.qwa_q40_qkv_projection
+        _track_packed(ctx, weight)
     else:
         _f16(weight, "weight", 4096 * k)
         fn = ctx.lib.qwa_qkv_projection

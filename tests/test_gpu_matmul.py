@@ -135,3 +135,23 @@ def test_fused_qkv_projection_q40_matches_oracle(pkg, oracle, cuda_dev):
         cos = np.sum(got * ref, -1) / (np.linalg.norm(got, axis=-1) * np.linalg.norm(ref, axis=-1))
         assert cos.min() >= 0.9999
     _check(v.cpu().numpy(), q40.matmul(x, w)[:, 3072:])
+
+
+def test_q40_cache_entry_dies_with_its_tensor(pkg, cuda_dev):
+    """A new packed matrix placed at a freed one's address must not be served
+    the old f16 copy (the wrapper forgets the copy when the tensor dies)."""
+    import gc
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(8)
+    m, n, k = 64, 256, 64
+    a = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float16)).cuda()
+    kern = mm.QuantMatmulKernel(0)
+    for trial in range(3):
+        packed = _packed(rng, n, k)
+        dp = torch.from_numpy(packed).cuda()
+        run = kern.create_run_from_buffers(a, dp, m, n, k)
+        kern.encode(None, run)
+        _check(run.output.cpu().numpy(),
+               q40.matmul(a.cpu().numpy(), q40.dequant_tile32(packed, n, k)))
+        del run, dp
+        gc.collect()
