@@ -160,7 +160,26 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&a)[32]) {
 // p = 2^(s*scale - m) for 32 raw scores; packs them as f16 pairs into a[0..15]
 // (in place, ascending, so every pair is read before its slot is reused) and
 // returns their fp32 sum.
+// exp2(a * scale - m) of 32 scores, packed to f16 pairs in a[0..15]; returns
+// their sum (even and odd columns summed separately, then added). The scale
+// and the sums run as paired f32 instructions (same rounding per lane).
 __device__ __forceinline__ float exp_pack_chunk(uint32_t (&a)[32], float scale, float m) {
+#ifndef QWA_NO_F32X2
+  const uint64_t s2 = f2_pack(scale, scale), nm2 = f2_pack(-m, -m);
+  uint64_t sum2 = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float y0, y1;
+    f2_unpack(fma2(f2_pack(__uint_as_float(a[2 * i]), __uint_as_float(a[2 * i + 1])), s2, nm2),
+              y0, y1);
+    const float e0 = ex2(y0), e1 = ex2(y1);
+    sum2 = add2(sum2, f2_pack(e0, e1));
+    a[i] = pack_half2(e0, e1);
+  }
+  float sum0, sum1;
+  f2_unpack(sum2, sum0, sum1);
+  return sum0 + sum1;
+#else
   float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -171,6 +190,7 @@ __device__ __forceinline__ float exp_pack_chunk(uint32_t (&a)[32], float scale, 
     a[i] = pack_half2(e0, e1);
   }
   return sum0 + sum1;
+#endif
 }
 
 __device__ __forceinline__ bool tile_needs_mask(const KeySchedule& s, int j, int ks, int q0,
@@ -442,8 +462,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(t_o + 32 * c, o);
             tmem_wait_ld();
             reg_fence32(o);
+#ifndef QWA_NO_F32X2
+            const uint64_t f2 = f2_pack(f, f);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float r0, r1;
+              f2_unpack(mul2(f2_pack(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1])), f2),
+                        r0, r1);
+              o[2 * i] = __float_as_uint(r0);
+              o[2 * i + 1] = __float_as_uint(r1);
+            }
+#else
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+#endif
             tmem_st32(t_o + 32 * c, o);
           }
         }
