@@ -309,8 +309,9 @@ qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void*
   Plan* plan = nullptr;
   st = get_plan(ctx, cu, batch, sparse, prefix, window, stream, &plan);
   if (st != QWA_OK) return st;
-  CUtensorMap tm_q, tm_k, tm_v;
+  CUtensorMap tm_q, tm_k, tm_v, tm_o;
   if ((st = make_map(ctx, &tm_q, q, kQHeads, total, kQHeads * kHeadDim * 2)) != QWA_OK) return st;
+  if ((st = make_map(ctx, &tm_o, out, kQHeads, total, kQHeads * kHeadDim * 2)) != QWA_OK) return st;
   if ((st = make_map(ctx, &tm_k, k, kKVHeads, total, kKVHeads * kHeadDim * 2)) != QWA_OK) return st;
   if ((st = make_map(ctx, &tm_v, v_base, kKVHeads, total, v_stride * 2)) != QWA_OK) return st;
   AttnArgs args;
@@ -322,7 +323,7 @@ qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void*
   args.scale_log2 = kScale * 1.4426950408889634f;
   args.status = ctx->d_status;
   args.trace = ctx->trace;
-  QWA_CUDA(ctx, launch_attention(tm_q, tm_k, tm_v, args, plan->n_items, stream));
+  QWA_CUDA(ctx, launch_attention(tm_q, tm_k, tm_v, tm_o, args, plan->n_items, stream));
   return QWA_OK;
 }
 

@@ -44,7 +44,8 @@ namespace {
 enum TraceEvent : int {
   kTrK = 0, kTrV, kTrMmaSA, kTrMmaPVB, kTrMmaSB, kTrMmaPVA,
   kTrSmSReady, kTrSmLoaded = kTrSmSReady + 2, kTrSmMax = kTrSmLoaded + 2,
-  kTrSmExp = kTrSmMax + 2, kTrSmArrive = kTrSmExp + 2, kTrEpi = kTrSmArrive + 2
+  kTrSmExp = kTrSmMax + 2, kTrSmArrive = kTrSmExp + 2, kTrEpi = kTrSmArrive + 2,
+  kTrEpiEnd = kTrEpi + 2
 };
 #define QWA_TR(ev, j)                                                                \
   do {                                                                               \
@@ -72,8 +73,9 @@ enum Bar : int {
   kSlotEmpty = kSlotFull + kSlots,   // +slot
   kSFull = kSlotEmpty + kSlots,      // +X
   kPFull = kSFull + 2,               // +X
-  kOFinal = kPFull + 2,
-  kNumBars = kOFinal + 1
+  kOFinal = kPFull + 2,              // +X: O_X of the item complete
+  kOStaged = kOFinal + 2,            // +X: O tile of head X staged in shared memory
+  kNumBars = kOStaged + 2
 };
 constexpr uint32_t kHolderOff = kBarOff + 8 * kNumBars;
 constexpr uint32_t kAbortOff = kHolderOff + 4;
@@ -207,7 +209,8 @@ __device__ __forceinline__ bool tile_needs_mask(const KeySchedule& s, int j, int
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, const AttnArgs args,
+                     const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_o, const AttnArgs args,
                      int num_items) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(kQFull + b), 1);
-      mbar_init(bar(kQEmpty + b), 1);
+      mbar_init(bar(kQEmpty + b), 2);  // one arrival per head's epilogue
     }
     for (int s = 0; s < kSlots; ++s) {
       mbar_init(bar(kSlotFull + s), 1);
@@ -234,12 +237,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kSFull + x), 1);
       mbar_init(bar(kPFull + x), 128);
     }
-    mbar_init(bar(kOFinal), 1);
+    for (int x = 0; x < 2; ++x) mbar_init(bar(kOFinal + x), 1);
+    for (int x = 0; x < 2; ++x) mbar_init(bar(kOStaged + x), 4);  // one arrival per warp
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_o);
   }
   if (warp == 1) {
     tmem_alloc(smem_addr(tmem_holder), kTmemCols);
@@ -259,8 +264,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int c = 0;  // K/V ring uses
       bool ok = true;
+      AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
       for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
-        const AttnItem item = args.items[it];
+        // the next item's descriptor is loaded one item ahead (a global load
+        // at every item boundary sat on each role's critical path)
+        const AttnItem item = next_item;
+        if (it + static_cast<int>(gridDim.x) < num_items) next_item = args.items[it + gridDim.x];
         const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
         const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
         const int qb = li & 1;
@@ -310,8 +319,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool have_prev = false;  // PV_B of the previous tile still to issue
       int prev_v = 0, prev_j = 0, prev_nk = 8;
       bool prev_last = false;
+      AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
       for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
-        const AttnItem item = args.items[it];
+        // the next item's descriptor is loaded one item ahead (a global load
+        // at every item boundary sat on each role's critical path)
+        const AttnItem item = next_item;
+        if (it + static_cast<int>(gridDim.x) < num_items) next_item = args.items[it + gridDim.x];
         const KeySchedule sch = make_key_schedule(item.y, item.z, sparse, prefix, window);
         const int q_last = (item.y + kBlockM < item.z ? item.y + kBlockM : item.z) - 1;
         const int qb = li & 1;
@@ -341,13 +354,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             QWA_TR(kTrMmaPVB, t - 1);
             issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0, prev_nk);
             tc_commit(bar(kSlotEmpty + prev_v));
-            if (prev_last) tc_commit(bar(kOFinal));
+            if (prev_last) tc_commit(bar(kOFinal + 1));
           }
           QWA_TR(kTrMmaSB, t);
           issue_qk(t_s[1], qbd, k_desc, idesc);
           tc_commit(bar(kSFull + 1));
           tc_commit(bar(kSlotEmpty + sk));
-          if (j == sch.n - 1) tc_commit(bar(kQEmpty + qb));
           if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
                                kDevTimeoutSlotFull)))
             break;
@@ -357,6 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           QWA_TR(kTrMmaPVA, t);
           issue_pv(t_o[0], t_s[0], v_desc0 + ((sv * kTileBytes) >> 4), j > 0, width / 16);
+          // head A's output is final here; its epilogue need not wait for B
+          if (j == sch.n - 1) tc_commit(bar(kOFinal + 0));
           have_prev = true;
           prev_v = sv;
           prev_j = j;
@@ -369,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0, prev_nk);
         tc_commit(bar(kSlotEmpty + prev_v));
-        tc_commit(bar(kOFinal));
+        tc_commit(bar(kOFinal + 1));
       }
     }
   } else {
@@ -383,8 +397,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale = args.scale_log2;
     bool ok = true;
     int t = 0;
+    int n_staged = 0;  // full query tiles this head has staged (kOStaged phase)
+    int q_release = -1;  // row 0: Q buffer to release once its O stores read it
+    AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
     for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
-      const AttnItem item = args.items[it];
+      const AttnItem item = next_item;
+      if (it + static_cast<int>(gridDim.x) < num_items) next_item = args.items[it + gridDim.x];
       const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
       const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
       const int q = q0 + row;
@@ -483,40 +501,106 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(bar(kPFull + x));
         if (row == 0) QWA_TR(kTrSmArrive + x, t);
+        if (q_release >= 0) {  // row 0 only: see the epilogue
+          bulk_wait_read();
+          mbar_arrive(bar(kQEmpty + q_release));
+          q_release = -1;
+        }
       }
       // Epilogue. O_X is read to registers (wait::ld) before this warpgroup's
       // next P arrival, which is what the next item's first PV_X waits for.
-      if (!ok || !(ok = mbar_wait(bar(kOFinal), li & 1, abort_flag, args.status,
+      if (!ok || !(ok = mbar_wait(bar(kOFinal + x), li & 1, abort_flag, args.status,
                                   kDevTimeoutOFinal)))
         break;
       tc_fence_after();
       if (row == 0) QWA_TR(kTrEpi + x, t - 1);
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-      const bool valid = q < len;
-      __half* dst = args.out + (static_cast<int64_t>(row0 + row) * kQHeads + 2 * g + x) * kHeadDim;
+      const int qb = li & 1;
+      if (q0 + kBlockM <= len) {
+        // Full query tile: O goes through this item's Q buffer (free: the
+        // last S MMAs that read it completed before kOFinal) in the 128-byte
+        // swizzled layout Q arrived in, then out with two TMA stores per head.
+        // The warp-wide direct stores this replaces touched 32 rows 4 KB apart
+        // per instruction.
+        const uint32_t obuf = sbase + kQOff + qb * kQBufBytes + x * kTileBytes;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(t_o + 32 * c, o);
-        tmem_wait_ld();
-        reg_fence32(o);
-        if (valid) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o + 32 * c, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+          const uint32_t half_base = obuf + (c >> 1) * kHalfBytes + row * 128;
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            uint4 w;
-            w.x = pack_half2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
-            w.y = pack_half2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
-            w.z = pack_half2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
-            w.w = pack_half2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
-            d4[v] = w;
+            const uint32_t unit = static_cast<uint32_t>((c & 1) * 4 + v) ^ (row & 7);
+            const uint32_t w0 = pack_half2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+            const uint32_t w1 = pack_half2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+            const uint32_t w2 = pack_half2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+            const uint32_t w3 = pack_half2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(half_base + unit * 16),
+                         "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                         : "memory");
           }
         }
+        // Each warp publishes its rows (proxy fence, then one arrival); only
+        // the storing thread waits, with a bounded wait, so no warp can be
+        // left waiting on one that has given up.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kOStaged + x));
+        if (row == 0) {
+          ok = mbar_wait(bar(kOStaged + x), n_staged & 1, abort_flag, args.status,
+                         kDevTimeoutOStaged);
+          if (ok) {
+            tma_store_3d(&tm_o, obuf, 0, 2 * g + x, row0);
+            tma_store_3d(&tm_o, obuf + kHalfBytes, 64, 2 * g + x, row0);
+            bulk_commit();
+            // The buffer may take a new Q only once the stores have read it.
+            // That Q is needed one item later, so the wait and the release
+            // happen after this head's next P arrival, off the epilogue.
+            q_release = qb;
+          }
+        }
+        // the warp leaves together (its tcgen05 loads are warp-collective)
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        ++n_staged;
+      } else {
+        // Last, partial tile of a request: rows past len belong to the next
+        // request, so only valid rows are stored, directly.
+        const bool valid = q < len;
+        __half* dst = args.out + (static_cast<int64_t>(row0 + row) * kQHeads + 2 * g + x) * kHeadDim;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_o + 32 * c, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+          if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_half2(__uint_as_float(o[8 * v + 0]) * inv_l, __uint_as_float(o[8 * v + 1]) * inv_l);
+              w.y = pack_half2(__uint_as_float(o[8 * v + 2]) * inv_l, __uint_as_float(o[8 * v + 3]) * inv_l);
+              w.z = pack_half2(__uint_as_float(o[8 * v + 4]) * inv_l, __uint_as_float(o[8 * v + 5]) * inv_l);
+              w.w = pack_half2(__uint_as_float(o[8 * v + 6]) * inv_l, __uint_as_float(o[8 * v + 7]) * inv_l);
+              d4[v] = w;
+            }
+          }
+        }
+        if (row == 0) mbar_arrive(bar(kQEmpty + qb));
       }
+      if (row == 0) QWA_TR(kTrEpiEnd + x, t - 1);
       tc_fence_before();
+    }
+    if (q_release >= 0) {
+      bulk_wait_read();
+      mbar_arrive(bar(kQEmpty + q_release));
     }
   }
 
+  bulk_wait_all();  // epilogue stores of the last items (no-op for other threads)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -619,7 +703,8 @@ __global__ void __launch_bounds__(128, 1)
 }  // namespace
 
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                             const CUtensorMap& tm_v, const AttnArgs& args, int num_items,
+                             const CUtensorMap& tm_v, const CUtensorMap& tm_o,
+                             const AttnArgs& args, int num_items,
                              cudaStream_t stream) {
   // function attributes and SM counts are per device
   static bool configured[kMaxDevices] = {};
@@ -639,7 +724,8 @@ cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
   if (num_items <= 0) return cudaSuccess;
   const int sm_count = sms[dev];
   const int grid = num_items < sm_count ? num_items : sm_count;  // persistent: one CTA per SM
-  attention_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, args, num_items);
+  attention_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, tm_o, args,
+                                                           num_items);
   return cudaGetLastError();
 }
 

@@ -86,8 +86,11 @@ constexpr int kTraceCtas = 4;
 constexpr int kTraceEvents = 20;
 constexpr int kTraceIters = 256;
 
+// tm_o: the output [T, 16, 128] with tm_q's geometry (full query tiles are
+// written with TMA stores).
 cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                             const CUtensorMap& tm_v, const AttnArgs& args, int num_items,
+                             const CUtensorMap& tm_v, const CUtensorMap& tm_o,
+                             const AttnArgs& args, int num_items,
                              cudaStream_t stream);
 
 cudaError_t launch_selftest_tile(const CUtensorMap& tm_a, const CUtensorMap& tm_b,

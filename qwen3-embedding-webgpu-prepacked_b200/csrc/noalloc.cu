@@ -130,8 +130,9 @@ extern "C" qwa_status qwa_attention_noalloc(const void* q, const void* k, const 
   int* status = reinterpret_cast<int*>(scratch);
   AttnItem* d_items = reinterpret_cast<AttnItem*>(scratch + kStatusBytes);
 
-  CUtensorMap tm_q, tm_k, tm_v;
+  CUtensorMap tm_q, tm_k, tm_v, tm_o;
   if (!map3d(&tm_q, q, kQHeads, total, kQHeads * kHeadDim * 2) ||
+      !map3d(&tm_o, out, kQHeads, total, kQHeads * kHeadDim * 2) ||
       !map3d(&tm_k, k, kKVHeads, total, kKVHeads * kHeadDim * 2) ||
       !map3d(&tm_v, v_base, kKVHeads, total, v_stride * 2))
     return QWA_ERR_CUDA;
@@ -151,7 +152,8 @@ extern "C" qwa_status qwa_attention_noalloc(const void* q, const void* k, const 
   args.scale_log2 = 0.08838834764831845f * 1.4426950408889634f;
   args.status = status;
   args.trace = nullptr;
-  if (launch_attention(tm_q, tm_k, tm_v, args, static_cast<int>(items.size()), s) != cudaSuccess)
+  if (launch_attention(tm_q, tm_k, tm_v, tm_o, args, static_cast<int>(items.size()), s) !=
+      cudaSuccess)
     return QWA_ERR_CUDA;
   return QWA_OK;
 }

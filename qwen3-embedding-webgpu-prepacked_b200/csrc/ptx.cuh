@@ -21,6 +21,7 @@ enum DeviceError : int {
   kDevTimeoutSFull = 0x104,
   kDevTimeoutPFull = 0x105,
   kDevTimeoutOFinal = 0x106,
+  kDevTimeoutOStaged = 0x107,
   kDevTimeoutGemmEmpty = 0x201,
   kDevTimeoutGemmFull = 0x202,
   kDevTimeoutAccEmpty = 0x203,
@@ -108,6 +109,33 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
+}
+
+// 3-D tiled TMA store from this CTA's shared memory (bulk-group completion).
+// c0 * element size must be a multiple of 16 bytes; no coordinate negative.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed bulk store of this thread has read its source.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk store of this thread is complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA) before a barrier that orders them with a bulk copy.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ------------------------------------------------- clusters (CTA pairs only)
