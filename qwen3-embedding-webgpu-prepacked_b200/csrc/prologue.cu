@@ -16,13 +16,18 @@
 namespace qwa {
 namespace {
 
-// Two warps per block: at 99 registers a thread, 64-thread blocks fill the
-// register file (20 warps per SM) where 256-thread blocks left 23% of it idle
-// (16 warps); more tokens' loads in flight: 5.66 vs 5.25 TB/s on 80,000 tokens.
+// Occupancy sets the bytes in flight, and so the bandwidth: 64-thread
+// blocks with at least 10 resident per SM cap a thread at 96 registers (no
+// spills) for 20 warps per SM, each with a token's 6 KB of loads in flight.
+// Measured on 80,000 tokens: 6.16 TB/s, against 5.25 TB/s with 256-thread
+// blocks (99 registers, 16 warps, a quarter of the register file idle).
 #ifndef QWA_PRO_WPB
 #define QWA_PRO_WPB 2
 #endif
 constexpr int kWarpsPerBlock = QWA_PRO_WPB;
+#ifndef QWA_PRO_MINB
+#define QWA_PRO_MINB 10
+#endif
 constexpr int kHeads = kQHeads + kKVHeads;  // 24
 constexpr int kLoads = kHeads / 2;          // 12
 
@@ -46,7 +51,7 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&x)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kWarpsPerBlock * 32, QWA_PRO_MINB)
     qk_norm_rope_kernel(const __half* __restrict__ qkv, int64_t stride,
                         const float* __restrict__ q_weight, const float* __restrict__ k_weight,
                         const float2* __restrict__ table, __half* __restrict__ q_out,
