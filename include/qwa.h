@@ -249,7 +249,9 @@ QWA_API qwa_status qwa_q40_qkv_projection(qwa_ctx *ctx, const void *input, const
                                           const int32_t *cu_seqlens_host, int batch, float eps,
                                           float theta, const float *rope_table, void *stream);
 
-/* Drop the context's f16 copies made from `packed` (synchronises the device). */
+/* Drop the context's f16 copies made from `packed`. Never synchronises (safe
+ * during stream capture): the memory is released by the next Q4_0 call made
+ * outside a capture, or by qwa_destroy. */
 QWA_API qwa_status qwa_q40_forget(qwa_ctx *ctx, const void *packed);
 
 #ifdef __cplusplus

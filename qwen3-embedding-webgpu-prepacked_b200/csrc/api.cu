@@ -62,6 +62,7 @@ struct qwa_ctx {
   std::vector<std::vector<int32_t>> plan_order;  // insertion order for eviction
   // f16 weights dequantised from Q4_0 tile32 buffers, keyed by (buffer, n, k)
   std::map<std::tuple<const void*, int, int>, __half*> weights;
+  std::vector<__half*> retired;  // forgotten copies, freed outside stream capture
   unsigned long long* trace = nullptr;           // QWA_TRACE builds only
 };
 
@@ -377,6 +378,8 @@ qwa_status qwa_destroy(qwa_ctx* ctx) {
     ctx->plans.clear();
     for (auto& w : ctx->weights) cudaFree(w.second);
     ctx->weights.clear();
+    for (__half* w : ctx->retired) cudaFree(w);
+    ctx->retired.clear();
     if (ctx->d_rope) cudaFree(ctx->d_rope);
     if (ctx->d_status) cudaFree(ctx->d_status);
   }
@@ -506,6 +509,14 @@ namespace {
 // f16 copy of a Q4_0 tile32 matrix owned by the context (made on first use).
 qwa_status cached_q40(qwa_ctx* ctx, const void* packed, int n, int k, cudaStream_t s,
                       __half** out) {
+  if (!ctx->retired.empty()) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone) {
+      // cudaFree waits for the device, so no launch still reads these
+      for (__half* w : ctx->retired) cudaFree(w);
+      ctx->retired.clear();
+    }
+  }
   const auto key = std::make_tuple(packed, n, k);
   auto it = ctx->weights.find(key);
   if (it != ctx->weights.end()) {
@@ -609,11 +620,12 @@ qwa_status qwa_q40_matmul(qwa_ctx* ctx, const void* input, const void* packed, v
 
 qwa_status qwa_q40_forget(qwa_ctx* ctx, const void* packed) {
   if (!ctx) return QWA_ERR_INVALID_ARG;
-  DeviceGuard guard(ctx->device);
-  QWA_CUDA(ctx, cudaDeviceSynchronize());
+  // No synchronisation or free here (this may run while a stream is being
+  // captured): the copies move to a list freed by the next Q4_0 call made
+  // outside a capture, or by qwa_destroy.
   for (auto it = ctx->weights.begin(); it != ctx->weights.end();) {
     if (std::get<0>(it->first) == packed) {
-      cudaFree(it->second);
+      ctx->retired.push_back(it->second);
       it = ctx->weights.erase(it);
     } else {
       ++it;
