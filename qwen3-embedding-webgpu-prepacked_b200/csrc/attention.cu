@@ -72,8 +72,9 @@ enum Bar : int {
   kSlotFull = kQEmpty + 2,           // +slot
   kSlotEmpty = kSlotFull + kSlots,   // +slot
   kSFull = kSlotEmpty + kSlots,      // +X
-  kPFull = kSFull + 2,               // +X
-  kOFinal = kPFull + 2,              // +X: O_X of the item complete
+  kPLo = kSFull + 2,                 // +X: P of keys 0..63 in TMEM
+  kPHi = kPLo + 2,                   // +X: P of keys 64..127 in TMEM
+  kOFinal = kPHi + 2,              // +X: O_X of the item complete
   kOStaged = kOFinal + 2,            // +X: O tile of head X staged in shared memory
   kNumBars = kOStaged + 2
 };
@@ -120,6 +121,18 @@ __device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint6
     if (kk < nk)
       mma_ts(d_tmem, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV,
              (accumulate || kk > 0) ? 1u : 0u);
+}
+// One half of PV: K steps 4*half .. 4*half+3 (keys 64*half .. 64*half+63),
+// whose P the softmax publishes separately (kPLo / kPHi).
+__device__ __forceinline__ void issue_pv_half(uint32_t d_tmem, uint32_t p_tmem, uint64_t v_desc,
+                                              bool accumulate, int nk, int half) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int kk = 4 * half + i;
+    if (kk < nk)
+      mma_ts(d_tmem, p_tmem + kk * 8, v_desc + ((kk * 2048) >> 4), kIdescPV,
+             (accumulate || kk > 0) ? 1u : 0u);
+  }
 }
 
 __device__ __forceinline__ uint32_t low_bits(int n) {
@@ -238,7 +251,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bar(kSFull + x), 1);
-      mbar_init(bar(kPFull + x), 128);
+      mbar_init(bar(kPLo + x), 128);
+      mbar_init(bar(kPHi + x), 128);
     }
     for (int x = 0; x < 2; ++x) mbar_init(bar(kOFinal + x), 1);
     for (int x = 0; x < 2; ++x) mbar_init(bar(kOStaged + x), 4);  // one arrival per warp
@@ -350,12 +364,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_qk(t_s[0], qa, k_desc, idesc);
           tc_commit(bar(kSFull + 0));
           if (have_prev) {
-            if (!(ok = mbar_wait(bar(kPFull + 1), (t - 1) & 1, abort_flag, args.status,
+            const uint64_t vd = v_desc0 + ((prev_v * kTileBytes) >> 4);
+            if (!(ok = mbar_wait(bar(kPLo + 1), (t - 1) & 1, abort_flag, args.status,
                                  kDevTimeoutPFull)))
               break;
             tc_fence_after();
             QWA_TR(kTrMmaPVB, t - 1);
-            issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0, prev_nk);
+            issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 0);
+            if (!(ok = mbar_wait(bar(kPHi + 1), (t - 1) & 1, abort_flag, args.status,
+                                 kDevTimeoutPFull)))
+              break;
+            tc_fence_after();
+            issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 1);
             tc_commit(bar(kSlotEmpty + prev_v));
             if (prev_last) tc_commit(bar(kOFinal + 1));
           }
@@ -366,12 +386,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
                                kDevTimeoutSlotFull)))
             break;
-          if (!(ok = mbar_wait(bar(kPFull + 0), t & 1, abort_flag, args.status,
-                               kDevTimeoutPFull)))
-            break;
-          tc_fence_after();
-          QWA_TR(kTrMmaPVA, t);
-          issue_pv(t_o[0], t_s[0], v_desc0 + ((sv * kTileBytes) >> 4), j > 0, width / 16);
+          {
+            const uint64_t vd = v_desc0 + ((sv * kTileBytes) >> 4);
+            if (!(ok = mbar_wait(bar(kPLo + 0), t & 1, abort_flag, args.status,
+                                 kDevTimeoutPFull)))
+              break;
+            tc_fence_after();
+            QWA_TR(kTrMmaPVA, t);
+            issue_pv_half(t_o[0], t_s[0], vd, j > 0, width / 16, 0);
+            if (!(ok = mbar_wait(bar(kPHi + 0), t & 1, abort_flag, args.status,
+                                 kDevTimeoutPFull)))
+              break;
+            tc_fence_after();
+            issue_pv_half(t_o[0], t_s[0], vd, j > 0, width / 16, 1);
+          }
           // head A's output is final here; its epilogue need not wait for B
           if (j == sch.n - 1) tc_commit(bar(kOFinal + 0));
           have_prev = true;
@@ -382,11 +410,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (ok && have_prev &&
-          mbar_wait(bar(kPFull + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
+          mbar_wait(bar(kPLo + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
+        const uint64_t vd = v_desc0 + ((prev_v * kTileBytes) >> 4);
         tc_fence_after();
-        issue_pv(t_o[1], t_s[1], v_desc0 + ((prev_v * kTileBytes) >> 4), prev_j > 0, prev_nk);
-        tc_commit(bar(kSlotEmpty + prev_v));
-        tc_commit(bar(kOFinal + 1));
+        issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 0);
+        if (mbar_wait(bar(kPHi + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
+          tc_fence_after();
+          issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 1);
+          tc_commit(bar(kSlotEmpty + prev_v));
+          tc_commit(bar(kOFinal + 1));
+        }
       }
     }
   } else {
@@ -464,26 +497,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (row == 0) QWA_TR(kTrSmMax + x, t);
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        // P is published in two halves so PV's first four K steps (keys
+        // 0..63) run on the tensor pipe while keys 64..127 are exponentiated.
         float sum = exp_pack_chunk(a0, scale, m_use) + exp_pack_chunk(a1, scale, m_use);
-        if (!narrow) sum += exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
-        l_run += sum;
-        if (row == 0) QWA_TR(kTrSmExp + x, t);
         tmem_st16(t_s + 0, a0);
         tmem_st16(t_s + 16, a1);
-        if (!narrow) {
-          tmem_st16(t_s + 32, a2);
-          tmem_st16(t_s + 48, a3);
-        }
         if (__any_sync(0xffffffffu, need)) {
-          // O_X(j-1) is complete (S_X(j) was committed after PV_X(j-1)) and
-          // PV_X(j) waits for the arrival below.
+          // O_X(j-1) is complete (S_X(j) was committed after PV_X(j-1)); the
+          // rescale precedes the first P arrival, so no PV_X(j) step sees it
+          // half done.
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
             tmem_ld32(t_o + 32 * c, o);
             tmem_wait_ld();
             reg_fence32(o);
-#ifndef QWA_NO_F32X2
             const uint64_t f2 = f2_pack(f, f);
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -493,16 +521,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               o[2 * i] = __float_as_uint(r0);
               o[2 * i + 1] = __float_as_uint(r1);
             }
-#else
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-#endif
             tmem_st32(t_o + 32 * c, o);
           }
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(kPFull + x));
+        mbar_arrive(bar(kPLo + x));
+        if (!narrow) {
+          sum += exp_pack_chunk(a2, scale, m_use) + exp_pack_chunk(a3, scale, m_use);
+          tmem_st16(t_s + 32, a2);
+          tmem_st16(t_s + 48, a3);
+          tmem_wait_st();
+          tc_fence_before();
+        }
+        l_run += sum;
+        if (row == 0) QWA_TR(kTrSmExp + x, t);
+        mbar_arrive(bar(kPHi + x));
         if (row == 0) QWA_TR(kTrSmArrive + x, t);
         if (q_release >= 0) {  // row 0 only: see the epilogue
           bulk_wait_read();
