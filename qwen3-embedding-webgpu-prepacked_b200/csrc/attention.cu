@@ -182,7 +182,6 @@ __device__ __forceinline__ float chunk_max(const uint32_t (&a)[32]) {
 // their sum (even and odd columns summed separately, then added). The scale
 // and the sums run as paired f32 instructions (same rounding per lane).
 __device__ __forceinline__ float exp_pack_chunk(uint32_t (&a)[32], float scale, float m) {
-#ifndef QWA_NO_F32X2
   const uint64_t s2 = f2_pack(scale, scale), nm2 = f2_pack(-m, -m);
   uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
@@ -197,18 +196,6 @@ __device__ __forceinline__ float exp_pack_chunk(uint32_t (&a)[32], float scale, 
   float sum0, sum1;
   f2_unpack(sum2, sum0, sum1);
   return sum0 + sum1;
-#else
-  float sum0 = 0.f, sum1 = 0.f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float e0 = ex2(fmaf(__uint_as_float(a[2 * i]), scale, -m));
-    const float e1 = ex2(fmaf(__uint_as_float(a[2 * i + 1]), scale, -m));
-    sum0 += e0;
-    sum1 += e1;
-    a[i] = pack_half2(e0, e1);
-  }
-  return sum0 + sum1;
-#endif
 }
 
 __device__ __forceinline__ bool tile_needs_mask(const KeySchedule& s, int j, int ks, int q0,
