@@ -461,11 +461,12 @@ qwa_status run_matmul(qwa_ctx* ctx, const void* input, const void* weight, void*
   qwa_status st = ensure_encode(ctx);
   if (st != QWA_OK) return st;
   const bool pair = gemm_pair(m);
-  CUtensorMap tm_a, tm_w;
+  CUtensorMap tm_a, tm_w, tm_out;
   if ((st = make_map_2d(ctx, &tm_a, input, k, m, 128)) != QWA_OK) return st;
   if ((st = make_map_2d(ctx, &tm_w, weight, k, n, kGemmWBoxRows(pair))) != QWA_OK) return st;
-  QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, static_cast<__half*>(output), m, n, k, ctx->d_status,
-                                pair, stream));
+  if ((st = make_map_2d(ctx, &tm_out, output, n, m, 32)) != QWA_OK) return st;
+  QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
+                                ctx->d_status, pair, stream));
   return QWA_OK;
 }
 

@@ -49,9 +49,12 @@ constexpr int kCuSmem = 1024;  // requests whose cu_seqlens are staged in shared
 constexpr int kGemmThreads = 320;
 constexpr int kEpiWarps = 8;
 
-// Shared-memory layout of one shape.
-template <bool kPair>
+// Shared-memory layout of one shape. The plain GEMM on CTA pairs stages its
+// output in shared memory for TMA stores (kTmaOut); the 32 KB this takes fit
+// beside six pipeline stages because it has none of the QKV epilogue's regions.
+template <bool kQkv, bool kPair>
 struct Layout {
+  static constexpr bool kTmaOut = kPair && !kQkv;
   static constexpr int kStages = kPair ? 6 : 4;
   static constexpr uint32_t kABytes = 128 * kBK * 2;                      // 16 KB
   static constexpr uint32_t kBBytes = (kPair ? 128 : 256) * kBK * 2;      // 16 / 32 KB
@@ -60,13 +63,17 @@ struct Layout {
   // barriers: full[S], empty[S], acc_full[2], acc_empty[2]
   static constexpr int kFull = 0, kEmpty = kStages, kAccFull = 2 * kStages,
                        kAccEmpty = 2 * kStages + 2, kNumBars = 2 * kStages + 4;
-  static constexpr uint32_t kNormWOff = kBarOff + 8 * kNumBars;     // 2 x 128 f32
-  static constexpr uint32_t kCuOff = kNormWOff + 2 * 128 * 4;       // kCuSmem + 1 ints
-  static constexpr uint32_t kXchOff = kCuOff + (kCuSmem + 4) * 4;   // 8 KB of partial sums
-  static constexpr uint32_t kPairOkOff = kXchOff + 4 * 2 * 2 * 128 * 4;
+  // the QKV epilogue's regions (empty for the plain GEMM)
+  static constexpr uint32_t kNormWOff = kBarOff + 8 * kNumBars;           // 2 x 128 f32
+  static constexpr uint32_t kCuOff = kNormWOff + (kQkv ? 2 * 128 * 4 : 0);  // kCuSmem + 1 ints
+  static constexpr uint32_t kXchOff = kCuOff + (kQkv ? (kCuSmem + 4) * 4 : 0);  // partial sums
+  static constexpr uint32_t kPairOkOff = kXchOff + (kQkv ? 4 * 2 * 2 * 128 * 4 : 0);
   static constexpr uint32_t kHolderOff = kPairOkOff + 8 * 4;
   static constexpr uint32_t kAbortOff = kHolderOff + 4;
-  static constexpr uint32_t kSmem = kAbortOff + 4 + 1024;  // + alignment slack
+  // output staging: 4 KB (32 rows x 64 columns, 128-byte swizzle) per epilogue warp
+  static constexpr uint32_t kOutOff = (kAbortOff + 4 + 1023) & ~1023u;
+  static constexpr uint32_t kOutBytes = kTmaOut ? kEpiWarps * 4096 : 0;
+  static constexpr uint32_t kSmem = kOutOff + kOutBytes + 1024;  // + alignment slack
   static_assert(kSmem <= 232448, "shared memory budget");
   static constexpr uint32_t kIdesc = idesc_f16_f32(kPair ? 256 : 128, kBN, false);
   static constexpr int kRowsPerTile = kPair ? 256 : 128;
@@ -162,9 +169,10 @@ __device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int su
 template <bool kQkv, bool kPair>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a,
-                    const __grid_constant__ CUtensorMap tm_w, __half* __restrict__ out, int M,
+                    const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_out, __half* __restrict__ out, int M,
                     int N, int K, int* status, const QkvEpilogue qkv) {
-  using L = Layout<kPair>;
+  using L = Layout<kQkv, kPair>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -335,6 +343,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                            : qkv.k_out + (static_cast<int64_t>(row) * 8 + head0) * 128;
         norm_rope_quarter(t_tile, half, sub, lane, norm_w + (is_q ? 0 : 128), tab, qkv.eps,
                           row < M, xch, dst);
+      } else if constexpr (L::kTmaOut) {
+        // 32 rows x 64 columns at a time through this warp's staging buffer
+        // (the swizzled layout of a 128-byte TMA box), then one TMA store: the
+        // direct stores below touch 32 rows per warp instruction, and their
+        // L1 traffic competed with the MMAs' operand reads (measured ~17%).
+        const uint32_t stage = sbase + L::kOutOff + (warp - 2) * 4096;
+        const int r0 = m0 + sub * 32;
+#pragma unroll 1
+        for (int b = 0; b < 2; ++b) {
+          uint32_t v0[32], v1[32];
+          tmem_ld32(t_cols + 64 * b, v0);
+          tmem_ld32(t_cols + 64 * b + 32, v1);
+          tmem_wait_ld();
+          reg_fence32(v0);
+          reg_fence32(v1);
+          if (lane == 0) bulk_wait_read();  // the previous store has read the buffer
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const uint32_t* src = u < 4 ? v0 + 8 * u : v1 + 8 * (u - 4);
+            const uint32_t w0 = pack_half2(__uint_as_float(src[0]), __uint_as_float(src[1]));
+            const uint32_t w1 = pack_half2(__uint_as_float(src[2]), __uint_as_float(src[3]));
+            const uint32_t w2 = pack_half2(__uint_as_float(src[4]), __uint_as_float(src[5]));
+            const uint32_t w3 = pack_half2(__uint_as_float(src[6]), __uint_as_float(src[7]));
+            const uint32_t addr = stage + lane * 128 + ((static_cast<uint32_t>(u) ^ (lane & 7)) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1),
+                         "r"(w2), "r"(w3)
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_out, stage, n0 + 128 * half + 64 * b, r0);  // rows >= M are clipped
+            bulk_commit();
+          }
+        }
       } else {
         __half* orow = kQkv ? qkv.v_out + static_cast<int64_t>(row) * 1024 + (n0 - 3072)
                             : out + static_cast<int64_t>(row) * N + n0;
@@ -368,6 +412,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   }
 
+  if (L::kTmaOut) bulk_wait_all();  // epilogue stores (no-op for threads without any)
   tc_fence_before();
   if (kPair) cluster_sync();  // no CTA leaves while its peer may still signal it
   else __syncthreads();
@@ -379,9 +424,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 template <bool kQkv, bool kPair>
-cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
-                        int N, int K, int* status, const QkvEpilogue& qkv, cudaStream_t stream) {
-  using L = Layout<kPair>;
+cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                        const CUtensorMap& tm_out, __half* out, int M, int N, int K, int* status,
+                        const QkvEpilogue& qkv, cudaStream_t stream) {
+  using L = Layout<kQkv, kPair>;
   static bool configured[kMaxDevices] = {};
   static int sm_count[kMaxDevices] = {};
   int dev = 0;
@@ -413,27 +459,31 @@ cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair>, tm_a, tm_w, out, M, N, K,
-                              status, qkv);
+    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair>, tm_a, tm_w, tm_out, out, M, N,
+                              K, status, qkv);
   }
   const int grid = tiles < sm_count[dev] ? tiles : sm_count[dev];
-  gemm_f16_kernel<kQkv, kPair><<<grid, kGemmThreads, L::kSmem, stream>>>(tm_a, tm_w, out, M, N,
-                                                                          K, status, qkv);
+  gemm_f16_kernel<kQkv, kPair><<<grid, kGemmThreads, L::kSmem, stream>>>(tm_a, tm_w, tm_out, out,
+                                                                          M, N, K, status, qkv);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
-                            int N, int K, int* status, bool pair, cudaStream_t stream) {
-  return pair ? launch_gemm<false, true>(tm_a, tm_w, out, M, N, K, status, QkvEpilogue{}, stream)
-              : launch_gemm<false, false>(tm_a, tm_w, out, M, N, K, status, QkvEpilogue{}, stream);
+cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                            const CUtensorMap& tm_out, __half* out, int M, int N, int K,
+                            int* status, bool pair, cudaStream_t stream) {
+  return pair ? launch_gemm<false, true>(tm_a, tm_w, tm_out, out, M, N, K, status, QkvEpilogue{},
+                                         stream)
+              : launch_gemm<false, false>(tm_a, tm_w, tm_out, out, M, N, K, status, QkvEpilogue{},
+                                          stream);
 }
 
 cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
                             const QkvEpilogue& qkv, int* status, bool pair, cudaStream_t stream) {
-  return pair ? launch_gemm<true, true>(tm_a, tm_w, nullptr, M, 4096, K, status, qkv, stream)
-              : launch_gemm<true, false>(tm_a, tm_w, nullptr, M, 4096, K, status, qkv, stream);
+  // the fused epilogue writes directly; tm_a stands in for the unused output map
+  return pair ? launch_gemm<true, true>(tm_a, tm_w, tm_a, nullptr, M, 4096, K, status, qkv, stream)
+              : launch_gemm<true, false>(tm_a, tm_w, tm_a, nullptr, M, 4096, K, status, qkv, stream);
 }
 
 }  // namespace qwa

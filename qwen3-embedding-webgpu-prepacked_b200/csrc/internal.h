@@ -118,8 +118,11 @@ constexpr int kMaxDevices = 64;
 // pairs (cta_group::2), for large M.
 constexpr int kGemmWBoxRows(bool pair) { return pair ? 128 : 256; }
 constexpr int kGemmPairMinRows = 4096;
-cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w, __half* out, int M,
-                            int N, int K, int* status, bool pair, cudaStream_t stream);
+// tm_out: the output C as a 2-D map {N, M}, box {64, 32}, 128-byte swizzle
+// (CTA-pair launches write through it with TMA).
+cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                            const CUtensorMap& tm_out, __half* out, int M, int N, int K,
+                            int* status, bool pair, cudaStream_t stream);
 
 // Fused attn_qkv projection epilogue: per-head Q/K RMSNorm + RoPE on the q/k
 // tiles, v written as [T, 1024]. Positions are row - cu[request(row)].
