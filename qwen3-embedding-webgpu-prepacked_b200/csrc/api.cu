@@ -137,6 +137,35 @@ qwa_status make_map_2d(qwa_ctx* ctx, CUtensorMap* map, const void* base, int64_t
   return QWA_OK;
 }
 
+// Output maps of the fused QKV epilogue: boxes of 32 elements x 32 rows
+// (64-byte rows, 64-byte swizzle). heads == 0: 2-D {inner, rows}; otherwise
+// 3-D {128, heads, rows} with a 256-byte head stride.
+qwa_status make_out_map(qwa_ctx* ctx, CUtensorMap* map, void* base, int64_t inner, int heads,
+                        int64_t rows, int64_t row_stride_bytes) {
+  CUresult r;
+  if (heads == 0) {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t elem[2] = {1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, elem,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(row_stride_bytes)};
+    cuuint32_t box[3] = {32, 1, 32};
+    cuuint32_t elem[3] = {1, 1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box, elem,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS)
+    return fail(ctx, QWA_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (%d)",
+                static_cast<int>(r));
+  return QWA_OK;
+}
+
 qwa_status check_cu(qwa_ctx* ctx, const int32_t* cu, int batch, int* total, int* max_len) {
   if (!cu) return fail(ctx, QWA_ERR_INVALID_ARG, "cu_seqlens_host is NULL");
   if (batch < 1) return fail(ctx, QWA_ERR_INVALID_ARG, "batch must be >= 1 (got %d)", batch);
@@ -571,7 +600,14 @@ qwa_status run_qkv_projection(qwa_ctx* ctx, const void* input, const void* weigh
   e.cu = plan->d_cu;
   e.batch = batch;
   e.eps = eps;
-  QWA_CUDA(ctx, launch_gemm_qkv(tm_a, tm_w, total, k, e, ctx->d_status, pair, s));
+  CUtensorMap tm_vo = tm_a, tm_qo = tm_a, tm_ko = tm_a;  // single-CTA launches store directly
+  if (pair) {
+    if ((st = make_out_map(ctx, &tm_vo, v_out, 1024, 0, total, 1024 * 2)) != QWA_OK) return st;
+    if ((st = make_out_map(ctx, &tm_qo, q_out, 128, 16, total, 16 * 128 * 2)) != QWA_OK) return st;
+    if ((st = make_out_map(ctx, &tm_ko, k_out, 128, 8, total, 8 * 128 * 2)) != QWA_OK) return st;
+  }
+  QWA_CUDA(ctx, launch_gemm_qkv(tm_a, tm_w, tm_vo, tm_qo, tm_ko, total, k, e, ctx->d_status, pair,
+                                s));
   return QWA_OK;
 }
 

@@ -49,13 +49,14 @@ constexpr int kCuSmem = 1024;  // requests whose cu_seqlens are staged in shared
 constexpr int kGemmThreads = 320;
 constexpr int kEpiWarps = 8;
 
-// Shared-memory layout of one shape. The plain GEMM on CTA pairs stages its
-// output in shared memory for TMA stores (kTmaOut); the 32 KB this takes fit
-// beside six pipeline stages because it has none of the QKV epilogue's regions.
+// Shared-memory layout of one shape. On CTA pairs the epilogue stages its
+// output in shared memory for TMA stores (kTmaOut, 4 KB per epilogue warp).
+// The plain GEMM keeps six pipeline stages beside that, having none of the QKV
+// epilogue's regions; the fused QKV GEMM drops to five.
 template <bool kQkv, bool kPair>
 struct Layout {
-  static constexpr bool kTmaOut = kPair && !kQkv;
-  static constexpr int kStages = kPair ? 6 : 4;
+  static constexpr bool kTmaOut = kPair;
+  static constexpr int kStages = kPair ? (kQkv ? 5 : 6) : 4;
   static constexpr uint32_t kABytes = 128 * kBK * 2;                      // 16 KB
   static constexpr uint32_t kBBytes = (kPair ? 128 : 256) * kBK * 2;      // 16 / 32 KB
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
@@ -106,10 +107,26 @@ __device__ __forceinline__ void pair_sync(int sub) {
 // four first-level sums of squares through shared memory; the sum is then
 // combined in the order of the prologue kernel's butterfly (dims in groups of
 // 8, xor 8, 4, 2, 1), so inv equals the prologue's bit for bit.
+// 64-byte-row staging (TMA SWIZZLE_64B layout: 16-byte chunk XOR (row / 2) % 4).
+__device__ __forceinline__ void stage_row64(uint32_t buf, int row, int chunk, uint32_t w0,
+                                            uint32_t w1, uint32_t w2, uint32_t w3) {
+  const uint32_t addr =
+      buf + row * 64 + ((static_cast<uint32_t>(chunk) ^ ((static_cast<uint32_t>(row) >> 1) & 3u)) << 4);
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0), "r"(w1), "r"(w2),
+               "r"(w3)
+               : "memory");
+}
+
+// kTma: instead of 16-byte stores to dst0, each head's two 32-dim segments of
+// the warp's 32 rows go through the warp's two 2 KB staging buffers (stage,
+// stage + 2048) and two TMA stores of boxes {32 dims, 1 head, 32 rows} at
+// (32c / 64 + 32c, head0 + hh, r0); tm is the q or k output map.
+template <bool kTma>
 __device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int sub, int lane,
                                                   const float* w, const float4 (&tab)[16],
                                                   float eps, bool valid, float* xch,
-                                                  __half* dst0) {
+                                                  __half* dst0, uint32_t stage,
+                                                  const CUtensorMap* tm, int head0, int r0) {
 #pragma unroll 1
   for (int hh = 0; hh < 2; ++hh) {
     uint32_t lo[32], hi[32];
@@ -143,7 +160,11 @@ __device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int su
     const float m0 = g0.x + g1.x, m1 = g0.y + g1.y, m2 = g0.z + g1.z, m3 = g0.w + g1.w;
     const float ss = (m0 + m2) + (m1 + m3);
     const float inv = 1.0f / sqrtf(ss * (1.0f / 128) + eps);
-    if (!valid) continue;
+    if (!kTma && !valid) continue;
+    if (kTma) {  // both buffers free: the previous head's / tile's stores have read them
+      if (lane == 0) bulk_wait_read();
+      __syncwarp();
+    }
     uint4* d4 = reinterpret_cast<uint4*>(dst0 + 128 * hh);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // 8 dims per 16-byte store
@@ -160,8 +181,22 @@ __device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int su
         lo_out[e] = pack_half2(fmaf(na0, cs.x, -1.f * nb0 * cs.y), fmaf(na1, cs.z, -1.f * nb1 * cs.w));
         hi_out[e] = pack_half2(fmaf(nb0, cs.x, 1.f * na0 * cs.y), fmaf(nb1, cs.z, 1.f * na1 * cs.w));
       }
-      d4[4 * c + q] = make_uint4(lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
-      d4[8 + 4 * c + q] = make_uint4(hi_out[0], hi_out[1], hi_out[2], hi_out[3]);
+      if (kTma) {
+        stage_row64(stage, lane, q, lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
+        stage_row64(stage + 2048, lane, q, hi_out[0], hi_out[1], hi_out[2], hi_out[3]);
+      } else {
+        d4[4 * c + q] = make_uint4(lo_out[0], lo_out[1], lo_out[2], lo_out[3]);
+        d4[8 + 4 * c + q] = make_uint4(hi_out[0], hi_out[1], hi_out[2], hi_out[3]);
+      }
+    }
+    if (kTma) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {  // rows >= M are clipped by the map
+        tma_store_3d(tm, stage, 32 * c, head0 + hh, r0);
+        tma_store_3d(tm, stage + 2048, 64 + 32 * c, head0 + hh, r0);
+        bulk_commit();
+      }
     }
   }
 }
@@ -170,7 +205,9 @@ template <bool kQkv, bool kPair>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_w,
-                    const __grid_constant__ CUtensorMap tm_out, __half* __restrict__ out, int M,
+                    const __grid_constant__ CUtensorMap tm_out,
+                    const __grid_constant__ CUtensorMap tm_qo,
+                    const __grid_constant__ CUtensorMap tm_ko, __half* __restrict__ out, int M,
                     int N, int K, int* status, const QkvEpilogue qkv) {
   using L = Layout<kQkv, kPair>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -341,8 +378,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int head0 = is_q ? 2 * nt : 2 * (nt - 8);
         __half* dst = is_q ? qkv.q_out + (static_cast<int64_t>(row) * 16 + head0) * 128
                            : qkv.k_out + (static_cast<int64_t>(row) * 8 + head0) * 128;
-        norm_rope_quarter(t_tile, half, sub, lane, norm_w + (is_q ? 0 : 128), tab, qkv.eps,
-                          row < M, xch, dst);
+        norm_rope_quarter<L::kTmaOut>(t_tile, half, sub, lane, norm_w + (is_q ? 0 : 128), tab,
+                                      qkv.eps, row < M, xch, dst,
+                                      sbase + L::kOutOff + (warp - 2) * 4096,
+                                      is_q ? &tm_qo : &tm_ko, head0, m0 + sub * 32);
+      } else if constexpr (L::kTmaOut && kQkv) {
+        // v tiles: 32 rows x 32 columns per box through the two 2 KB buffers
+        const uint32_t stage = sbase + L::kOutOff + (warp - 2) * 4096;
+        const int r0 = m0 + sub * 32;
+#pragma unroll 1
+        for (int b = 0; b < 4; ++b) {
+          uint32_t v[32];
+          tmem_ld32(t_cols + 32 * b, v);
+          tmem_wait_ld();
+          reg_fence32(v);
+          if (lane == 0) {
+            if (b < 2) bulk_wait_read();  // earlier tiles' stores
+            else bulk_wait_read_but_one();  // the store of box b - 2
+          }
+          __syncwarp();
+          const uint32_t buf = stage + (b & 1) * 2048;
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            stage_row64(buf, lane, u,
+                        pack_half2(__uint_as_float(v[8 * u + 0]), __uint_as_float(v[8 * u + 1])),
+                        pack_half2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
+                        pack_half2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
+                        pack_half2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_out, buf, n0 - 3072 + 128 * half + 32 * b, r0);
+            bulk_commit();
+          }
+        }
       } else if constexpr (L::kTmaOut) {
         // 32 rows x 64 columns at a time through this warp's staging buffer
         // (the swizzled layout of a 128-byte TMA box), then one TMA store: the
@@ -425,7 +494,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 template <bool kQkv, bool kPair>
 cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
-                        const CUtensorMap& tm_out, __half* out, int M, int N, int K, int* status,
+                        const CUtensorMap& tm_out, const CUtensorMap& tm_qo,
+                        const CUtensorMap& tm_ko, __half* out, int M, int N, int K, int* status,
                         const QkvEpilogue& qkv, cudaStream_t stream) {
   using L = Layout<kQkv, kPair>;
   static bool configured[kMaxDevices] = {};
@@ -459,12 +529,12 @@ cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair>, tm_a, tm_w, tm_out, out, M, N,
-                              K, status, qkv);
+    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair>, tm_a, tm_w, tm_out, tm_qo, tm_ko,
+                              out, M, N, K, status, qkv);
   }
   const int grid = tiles < sm_count[dev] ? tiles : sm_count[dev];
-  gemm_f16_kernel<kQkv, kPair><<<grid, kGemmThreads, L::kSmem, stream>>>(tm_a, tm_w, tm_out, out,
-                                                                          M, N, K, status, qkv);
+  gemm_f16_kernel<kQkv, kPair><<<grid, kGemmThreads, L::kSmem, stream>>>(
+      tm_a, tm_w, tm_out, tm_qo, tm_ko, out, M, N, K, status, qkv);
   return cudaGetLastError();
 }
 
@@ -473,17 +543,21 @@ cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
 cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
                             const CUtensorMap& tm_out, __half* out, int M, int N, int K,
                             int* status, bool pair, cudaStream_t stream) {
-  return pair ? launch_gemm<false, true>(tm_a, tm_w, tm_out, out, M, N, K, status, QkvEpilogue{},
-                                         stream)
-              : launch_gemm<false, false>(tm_a, tm_w, tm_out, out, M, N, K, status, QkvEpilogue{},
-                                          stream);
+  // tm_out stands in for the q / k maps, which the plain epilogue never uses
+  return pair ? launch_gemm<false, true>(tm_a, tm_w, tm_out, tm_out, tm_out, out, M, N, K, status,
+                                         QkvEpilogue{}, stream)
+              : launch_gemm<false, false>(tm_a, tm_w, tm_out, tm_out, tm_out, out, M, N, K, status,
+                                          QkvEpilogue{}, stream);
 }
 
-cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
-                            const QkvEpilogue& qkv, int* status, bool pair, cudaStream_t stream) {
-  // the fused epilogue writes directly; tm_a stands in for the unused output map
-  return pair ? launch_gemm<true, true>(tm_a, tm_w, tm_a, nullptr, M, 4096, K, status, qkv, stream)
-              : launch_gemm<true, false>(tm_a, tm_w, tm_a, nullptr, M, 4096, K, status, qkv, stream);
+cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                            const CUtensorMap& tm_vo, const CUtensorMap& tm_qo,
+                            const CUtensorMap& tm_ko, int M, int K, const QkvEpilogue& qkv,
+                            int* status, bool pair, cudaStream_t stream) {
+  return pair ? launch_gemm<true, true>(tm_a, tm_w, tm_vo, tm_qo, tm_ko, nullptr, M, 4096, K,
+                                        status, qkv, stream)
+              : launch_gemm<true, false>(tm_a, tm_w, tm_vo, tm_qo, tm_ko, nullptr, M, 4096, K,
+                                         status, qkv, stream);
 }
 
 }  // namespace qwa

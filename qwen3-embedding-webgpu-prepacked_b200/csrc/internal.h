@@ -138,9 +138,13 @@ struct QkvEpilogue {
   float eps = 0.f;
 };
 
-// QKV projection (N = 4096) with the QkvEpilogue; K % 64 == 0.
-cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w, int M, int K,
-                            const QkvEpilogue& qkv, int* status, bool pair, cudaStream_t stream);
+// QKV projection (N = 4096) with the QkvEpilogue; K % 64 == 0. CTA-pair
+// launches write through TMA maps with 32 x 32 boxes and 64-byte swizzle:
+// tm_vo 2-D {1024, M}; tm_qo / tm_ko 3-D {128 dims, 16 / 8 heads, M}.
+cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                            const CUtensorMap& tm_vo, const CUtensorMap& tm_qo,
+                            const CUtensorMap& tm_ko, int M, int K, const QkvEpilogue& qkv,
+                            int* status, bool pair, cudaStream_t stream);
 
 // Q4_0 tile32-compact records (20 bytes: f16 scale, 2 pad bytes, 16 bytes of
 // nibbles) -> f16 W[n, k] row-major.
