@@ -47,7 +47,8 @@ enum TraceEvent : int {
   kTrK = 0, kTrV, kTrMmaSA, kTrMmaPVB, kTrMmaSB, kTrMmaPVA,
   kTrSmSReady, kTrSmLoaded = kTrSmSReady + 2, kTrSmMax = kTrSmLoaded + 2,
   kTrSmExp = kTrSmMax + 2, kTrSmArrive = kTrSmExp + 2, kTrEpi = kTrSmArrive + 2,
-  kTrEpiEnd = kTrEpi + 2
+  kTrEpiEnd = kTrEpi + 2, kTrMmaPHiA = kTrEpiEnd + 2, kTrMmaKWait, kTrMmaPHiB,
+  kTrMmaPVAHiDone, kTrMmaSADone
 };
 #define QWA_TR(ev, j)                                                                \
   do {                                                                               \
@@ -216,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int ck = 2 * t, sk = ck % kSlots;
           const int cv = 2 * t + 1, sv = cv % kSlots;
           const uint64_t k_desc = k_desc0 + ((sk * kTileBytes) >> 4);
+          QWA_TR(kTrMmaKWait, t);
           if (!(ok = mbar_wait(bar(kSlotFull + sk), (ck / kSlots) & 1, abort_flag, args.status,
                                kDevTimeoutSlotFull)))
             break;
@@ -224,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int width = key_tile_width(sch, j, q_last, prefix);
           const uint32_t idesc = idesc_f16_f32(128, width, false);
           issue_qk(t_s[0], qa, k_desc, idesc);
+          QWA_TR(kTrMmaSADone, t);
           tc_commit(bar(kSFull + 0));
           if (have_prev) {
             const uint64_t vd = v_desc0 + ((prev_v * kTileBytes) >> 4);
@@ -237,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  kDevTimeoutPFull)))
               break;
             tc_fence_after();
+            QWA_TR(kTrMmaPHiB, t - 1);
             issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 1);
             tc_commit(bar(kSlotEmpty + prev_v));
             if (prev_last) tc_commit(bar(kOFinal + 1));
@@ -260,7 +264,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  kDevTimeoutPFull)))
               break;
             tc_fence_after();
+            QWA_TR(kTrMmaPHiA, t);
             issue_pv_half(t_o[0], t_s[0], vd, j > 0, width / 16, 1);
+            QWA_TR(kTrMmaPVAHiDone, t);
           }
           // head A's output is final here; its epilogue need not wait for B
           if (j == sch.n - 1) tc_commit(bar(kOFinal + 0));

@@ -83,7 +83,7 @@ struct AttnArgs {
 // kTraceIters + key_tile] = clock64() for the first kTraceCtas CTAs (key_tile
 // counts the CTA's tiles across its work items).
 constexpr int kTraceCtas = 4;
-constexpr int kTraceEvents = 20;
+constexpr int kTraceEvents = 25;
 constexpr int kTraceIters = 256;
 
 // tm_o: the output [T, 16, 128] with tm_q's geometry (full query tiles are
