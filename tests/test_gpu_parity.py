@@ -129,6 +129,67 @@ def test_attention_parity(pkg, oracle, cuda_dev, lengths, mode, prefix, window):
     _check(out.cpu().numpy(), ref, f"attention {lengths} mode {mode}")
 
 
+@pytest.mark.parametrize("mode", [1, 2])
+def test_attention_parity_large_scores(pkg, oracle, cuda_dev, mode):
+    """q and k scaled by 4 and 3: scores spread ~12x wider, so the running
+    max often grows by more than 2^8 from one key tile to the next and the
+    lazy O rescale runs on many tiles (near one-hot softmax rows).
+
+    Outside the contract's input distribution (the prologue RMS-normalises
+    q and k), so the bound is the one f16 arithmetic allows there: a
+    near one-hot row returns ~V with |V| up to ~4.5, where the f16 output
+    spacing is 1.95e-3 to 3.9e-3. Output rounding costs up to half a spacing,
+    and P rounded to f16 for the PV MMA (with the row sum taken in f32) up to
+    one more. Bound: max(2e-3, 1.5 f16 spacings of the reference value)."""
+    lengths = [1500, 700]
+    rng = np.random.default_rng(77 + mode)
+    cu = [0] + [int(x) for x in np.cumsum(lengths)]
+    T = cu[-1]
+    q = (4 * rng.standard_normal((T, 16, 128), dtype=np.float32)).astype(np.float16)
+    k = (3 * rng.standard_normal((T, 8, 128), dtype=np.float32)).astype(np.float16)
+    v = rng.standard_normal((T, 1024), dtype=np.float32).astype(np.float16)
+    out = pkg.attention.attention(_dev(q), _dev(k), _dev(v), cu, 1024, 0, mode)
+    pkg.attention.Context.for_device(0).check()
+    ref = oracle.c_attention(q, k, v, 1024, 0, cu, mode)
+    got = out.cpu().numpy().astype(np.float64)
+    assert np.isfinite(got).all()
+    bound = np.maximum(MAX_ABS, 1.5 * np.spacing(np.abs(ref).astype(np.float16)).astype(np.float64))
+    excess = (np.abs(got - ref) - bound).max()
+    assert excess <= 0, f"large scores mode {mode}: error exceeds its bound by {excess:.3e}"
+    for h in range(16):
+        a, b = got[:, h].ravel(), ref[:, h].ravel()
+        assert a @ b / (np.linalg.norm(a) * np.linalg.norm(b)) >= MIN_COS
+
+
+def test_auto_mode_above_8192_is_full_causal(pkg, oracle, cuda_dev):
+    """Above 8192 tokens the reference dispatches its chunked full-causal
+    path instead of the sparse tiled one (src/webgpu/ops.ts:328): AUTO must
+    give exactly FULL's output there, and the oracle's full-causal rows."""
+    lengths = [8193, 300]
+    cu = [0] + [int(x) for x in np.cumsum(lengths)]
+    T = cu[-1]
+    g = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn(T, 16, 128, generator=g, device="cuda").half()
+    k = torch.randn(T, 8, 128, generator=g, device="cuda").half()
+    v = torch.randn(T, 1024, generator=g, device="cuda").half()
+    attn = pkg.attention
+    out_auto = attn.attention(q, k, v, cu, 1024, 0, 0)
+    out_full = attn.attention(q, k, v, cu, 1024, 0, 1)
+    out_sparse = attn.attention(q, k, v, cu, 1024, 0, 2)
+    attn.Context.for_device(0).check()
+    assert torch.equal(out_auto, out_full)
+    # past 608 keys the sparse rule drops pairs, so it must differ there
+    assert not torch.equal(out_auto[700:8193], out_sparse[700:8193])
+    rng = np.random.default_rng(5)
+    toks = np.concatenate([rng.integers(0, T, 96), [0, 607, 608, 8191, 8192, 8193, T - 1]])
+    rows = np.unique(toks[:, None] * 16 + rng.integers(0, 16, (len(toks), 2))).astype(np.int64)
+    ref = oracle.c_attention_rows(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), 1024, 0, cu,
+                                  rows, 0)
+    got = out_auto.view(T * 16, 128)[torch.from_numpy(rows).cuda()].cpu().numpy()
+    err = np.abs(got.astype(np.float64) - ref).max()
+    assert err <= MAX_ABS, err
+
+
 def test_ragged_layer_parity_config2(pkg, oracle, cuda_dev):
     w = pkg.workloads.WORKLOADS["c2_ragged16"]
     cu = w.cu_seqlens()
