@@ -71,21 +71,34 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
-    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+    """nvidia-smi clocks / throttle reasons, sampled every 50 ms from before
+    the warm-up on. mark_start() / mark_end() bracket the timed region, and
+    summary() uses the samples taken inside it (±50 ms), or all samples,
+    flagged, if the region was too short to catch one."""
+    Q = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
 
     def __init__(self, index: int):
         self.index = index
-        self.rows = []
+        self.rows = []  # (datetime or None, [fields after the timestamp])
+        self.window = [None, None]
         self._stop = threading.Event()
         self._t = None
+
+    @staticmethod
+    def _time(text):
+        import datetime
+        try:
+            return datetime.datetime.strptime(text.strip(), "%Y/%m/%d %H:%M:%S.%f")
+        except ValueError:
+            return None
 
     def _run(self):
         try:
             p = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                  "--format=csv,noheader,nounits", "-lms", "200"],
+                                  "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS)],
                                  stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             return
@@ -93,12 +106,21 @@ class ClockSampler:
             line = p.stdout.readline()
             if not line:
                 break
-            self.rows.append([x.strip() for x in line.split(",")])
+            f = [x.strip() for x in line.split(",")]
+            self.rows.append((self._time(f[0]), f[1:]))
         p.terminate()
         try:
             p.wait(timeout=5)
         except subprocess.TimeoutExpired:
             p.kill()
+
+    def mark_start(self):
+        import datetime
+        self.window[0] = datetime.datetime.now()
+
+    def mark_end(self):
+        import datetime
+        self.window[1] = datetime.datetime.now()
 
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
@@ -110,17 +132,27 @@ class ClockSampler:
         self._t.join(timeout=10)
 
     def summary(self):
-        if not self.rows:
+        import datetime
+        rows, scope = [r for _, r in self.rows], "whole run"
+        if self.window[0] and self.window[1]:
+            pad = datetime.timedelta(milliseconds=self.INTERVAL_MS)
+            inside = [r for t, r in self.rows
+                      if t is not None and self.window[0] - pad <= t <= self.window[1] + pad]
+            if inside:
+                rows, scope = inside, "timed region"
+            else:
+                scope = "whole run (no sample inside the timed region)"
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
+        reasons = sorted({names[i] for r in rows for i in range(4)
                           if len(r) > 3 + i and r[3 + i] == "Active"})
         loaded = sorted(sm)[len(sm) // 4:] if sm else []
         return {"sm_mhz": float(np.median(loaded)) if loaded else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+                "samples": len(rows), "scope": scope}
 
 
 def dist_setup(gpus: int):
@@ -489,15 +521,22 @@ def main():
     ctx.check(stream)
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
+        # the sampler is up (and the clocks settled under load) before timing
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                graph.replay()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        clocks.mark_start()
         with torch.cuda.stream(stream):
             start.record(stream)
             for _ in range(args.steps):
                 graph.replay()
             end.record(stream)
         torch.cuda.synchronize()
+        clocks.mark_end()
     barrier()
     ctx.check(stream)
     ms = start.elapsed_time(end) / args.steps
