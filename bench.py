@@ -143,7 +143,8 @@ class ClockSampler:
             else:
                 scope = "whole run (no sample inside the timed region)"
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"],
+                    "samples": 0, "scope": scope}
         sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
         mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
