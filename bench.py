@@ -7,10 +7,13 @@ layers, the fused Q/K RMSNorm + RoPE prologue and the causal/sparse GQA
 attention (the two runs Qwen3ExecutionPlan encodes per layer,
 src/webgpu/model.ts:94-95), each layer with its own seeded inputs.
 
-Multi-GPU (torchrun, one process per GPU): requests are independent, so
-every rank runs its own micro-batch of the workload (weak scaling) with no
-collective on the hot path; the barrier + max-over-ranks timing only frame
-the measurement. ``value`` = tokens of all ranks / max step time.
+Multi-GPU (torchrun, one process per GPU): requests are independent, so the
+workload's requests are split across the ranks (LPT on kept pairs; strong
+scaling), each rank runs its share as one packed micro-batch, and the e2e leg
+gathers every rank's output rows into one shared host buffer in request
+order. No collective is on the hot path; the barrier and the max-over-ranks
+timing only frame the measurement. ``value`` = the workload's tokens / max
+step time. ``--weak-scaling`` gives every rank the whole workload instead.
 
 ``--impl reference``: the reference's hot path exists only as WGSL for a
 browser WebGPU (unavailable on this box), so this arm times the CPU oracle
@@ -48,6 +51,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--weak-scaling", action="store_true",
+                    help="every rank runs the whole workload (default: the workload's requests "
+                         "are split across the ranks)")
     ap.add_argument("--gemm", action="store_true",
                     help="time the projection GEMM against cuBLAS and the fused QKV projection")
     ap.add_argument("--gemm-rows", type=int, default=0,
@@ -224,7 +230,7 @@ def run_reference(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": w.name, "requests": len(w.lengths), "seq_len": L,
                    "layers": w.layers, "mode": w.mode,
@@ -452,6 +458,7 @@ def main():
     import torch
     pkg = importlib.import_module(PKG)
     attn = pkg.attention
+    ex = pkg.executor
     lib = pkg._lib.load()
     w = pkg.workloads.WORKLOADS[args.workload]
     if args.requests or args.layers:
@@ -463,18 +470,28 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     ctx = attn.Context.for_device(local)
-    cu = w.cu_seqlens()
+    # Strong scaling (default): the workload's requests are split across the
+    # ranks (LPT on kept pairs), each rank runs its share as one packed
+    # micro-batch. --weak-scaling: every rank runs the whole workload.
+    plan = ex.ShardPlan(w.lengths, 1 if args.weak_scaling else world, w.mode)
+    me = 0 if args.weak_scaling else rank
+    cu = plan.local_cu(me)
     cu_c = pkg._lib.cu_array(cu)
-    T = w.tokens
+    T = plan.local_tokens(me)
+    T_all = plan.total_tokens * (world if args.weak_scaling else 1)
+    mode = plan.resolved_mode  # AUTO resolved on the whole micro-batch
     L = w.layers
+    idle = T == 0
 
-    # inputs resident in HBM: one qkv activation per layer (each > L2, so
-    # consecutive layers never hit in L2), per-layer norm weights
-    layers = [pkg.workloads.device_layer_inputs(T, seed=1000 * rank + l, device=dev)
+    # inputs resident in HBM: one qkv activation per layer (each > L2 at the
+    # default workload, so consecutive layers never hit in L2), per-layer
+    # norm weights
+    layers = [pkg.workloads.device_layer_inputs(max(T, 1), seed=1000 * rank + l, device=dev)
               for l in range(L)]
-    q_buf = torch.empty(T, 16, 128, dtype=torch.float16, device=dev)
-    k_buf = torch.empty(T, 8, 128, dtype=torch.float16, device=dev)
-    out = torch.empty(T, 16, 128, dtype=torch.float16, device=dev)
+    Tb = max(T, 1)
+    q_buf = torch.empty(Tb, 16, 128, dtype=torch.float16, device=dev)
+    k_buf = torch.empty(Tb, 8, 128, dtype=torch.float16, device=dev)
+    out = torch.empty(Tb, 16, 128, dtype=torch.float16, device=dev)
     stream = torch.cuda.Stream(dev)
     s = stream.cuda_stream
     P = attn._ptr
@@ -488,13 +505,15 @@ def main():
         if ev is not None:
             ev[0].record(stream)
         st = lib.qwa_attention(ctx.handle, P(q_buf), P(k_buf), P(qkv), 4096, 3072, P(o), cu_c,
-                               len(cu) - 1, w.mode, 176, 432, s)
+                               len(cu) - 1, mode, 176, 432, s)
         if st:
             pkg._lib.check(st, ctx.handle)
         if ev is not None:
             ev[1].record(stream)
 
     def step(evs=None):
+        if idle:
+            return
         for l, (qkv, qw, kw) in enumerate(layers):
             layer_calls(qkv, qw, kw, evs[l] if evs is not None else None)
 
@@ -514,19 +533,24 @@ def main():
     # warm-up every call is capture-safe: plans are cached and tensor maps are
     # encoded on the host.
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step()
-    with torch.cuda.stream(stream):
-        graph.replay()
+    if not idle:
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        with torch.cuda.stream(stream):
+            graph.replay()
     torch.cuda.synchronize()
     ctx.check(stream)
+
+    def replay():
+        if not idle:
+            graph.replay()
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         # the sampler is up (and the clocks settled under load) before timing
         with torch.cuda.stream(stream):
             for _ in range(max(1, args.warmup)):
-                graph.replay()
+                replay()
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
@@ -534,7 +558,7 @@ def main():
         with torch.cuda.stream(stream):
             start.record(stream)
             for _ in range(args.steps):
-                graph.replay()
+                replay()
             end.record(stream)
         torch.cuda.synchronize()
         clocks.mark_end()
@@ -548,83 +572,38 @@ def main():
                 for _ in range(args.steps)]
     ev_pro_start = [[torch.cuda.Event(enable_timing=True) for _ in range(L)]
                     for _ in range(args.steps)]
-    for kstep in range(args.steps):
-        for l, (qkv, qw, kw) in enumerate(layers):
-            ev_pro_start[kstep][l].record(stream)
-            layer_calls(qkv, qw, kw, ev_layer[kstep][l])
-    torch.cuda.synchronize()
-    ctx.check(stream)
-    attn_ms = [ev_layer[k][l][0].elapsed_time(ev_layer[k][l][1])
-               for k in range(args.steps) for l in range(L)]
-    pro_ms = [ev_pro_start[k][l].elapsed_time(ev_layer[k][l][0])
-              for k in range(args.steps) for l in range(L)]
+    attn_ms, pro_ms = [0.0], [0.0]
+    if not idle:
+        for kstep in range(args.steps):
+            for l, (qkv, qw, kw) in enumerate(layers):
+                ev_pro_start[kstep][l].record(stream)
+                layer_calls(qkv, qw, kw, ev_layer[kstep][l])
+        torch.cuda.synchronize()
+        ctx.check(stream)
+        attn_ms = [ev_layer[k][l][0].elapsed_time(ev_layer[k][l][1])
+                   for k in range(args.steps) for l in range(L)]
+        pro_ms = [ev_pro_start[k][l].elapsed_time(ev_layer[k][l][0])
+                  for k in range(args.steps) for l in range(L)]
+    rank_ms = [ms]
     if world > 1:
         import torch.distributed as dist
         t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        gathered = [torch.zeros(1, device=dev) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        rank_ms = [float(x.item()) for x in gathered]
+        ms = max(rank_ms)
 
-    # end to end through the C ABI with host buffers: every layer's qkv
-    # crosses host->device from pinned memory, the layer output comes back
+    # End to end through the package's request-sharded executor, with host
+    # buffers: every layer's qkv rows of this rank's requests cross
+    # host->device from page-locked memory, and the layer's output rows come
+    # back into one host output buffer at their requests' rows (the host
+    # gather; with several ranks the buffers are shared memory that every
+    # rank maps). Uploads, kernels and downloads of consecutive layers
+    # overlap (double-buffered, ordered by events; PCIe is full duplex).
     e2e = None
     if not args.no_e2e:
-        # Pipelined over layers: H2D of layer l+1 and D2H of layer l-1 run on
-        # their own streams while layer l computes (double-buffered device
-        # inputs and outputs, ordered by events); PCIe is full duplex.
-        host_in = [torch.empty(T, 4096, dtype=torch.float16).pin_memory() for _ in range(2)]
-        for h in host_in:
-            h.copy_(layers[0][0].cpu())
-        host_out = [torch.empty(T, 16, 128, dtype=torch.float16).pin_memory() for _ in range(2)]
-        dev_in = [torch.empty(T, 4096, dtype=torch.float16, device=dev) for _ in range(2)]
-        dev_out = [torch.empty(T, 16, 128, dtype=torch.float16, device=dev) for _ in range(2)]
-        h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-        def e2e_step():
-            in_free = [None, None]   # compute done with dev_in[b]
-            out_free = [None, None]  # D2H done with dev_out[b]
-            for l in range(L):
-                b = l % 2
-                with torch.cuda.stream(h2d):
-                    if in_free[b] is not None:
-                        h2d.wait_event(in_free[b])
-                    dev_in[b].copy_(host_in[b], non_blocking=True)
-                    ready = torch.cuda.Event()
-                    ready.record(h2d)
-                stream.wait_event(ready)
-                if out_free[b] is not None:
-                    stream.wait_event(out_free[b])
-                layer_calls(dev_in[b], layers[l][1], layers[l][2], out_buf=dev_out[b])
-                done = torch.cuda.Event()
-                done.record(stream)
-                in_free[b] = done
-                with torch.cuda.stream(d2h):
-                    d2h.wait_event(done)
-                    host_out[b].copy_(dev_out[b], non_blocking=True)
-                    freed = torch.cuda.Event()
-                    freed.record(d2h)
-                    out_free[b] = freed
-            # the step ends when its last output is on the host
-            stream.wait_event(out_free[(L - 1) % 2])
-
-        e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        e0.record(stream)
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
-        if world > 1:
-            import torch.distributed as dist
-            t = torch.tensor([e2e_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-        e2e = {"value": world * T / (e2e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": T * 4096 * 2 * L,
-               "d2h_bytes_per_step": T * 2048 * 2 * L, "ms_per_step": e2e_ms}
+        e2e = run_e2e(args, torch, ex, plan, me, world, rank, local, dev, layers, ctx, barrier,
+                      T, T_all, L)
 
     if rank != 0:
         if world > 1:
@@ -633,36 +612,55 @@ def main():
         return
 
     peaks, src = measured_peaks()
-    pairs, tiles = attn.attention_work(cu, w.mode)
+    pairs, tiles = attn.attention_work(cu, mode) if not idle else (0, 0)
     flop_per_launch = 8192.0 * pairs
     attn_avg = float(np.mean(attn_ms))
     pro_avg = float(np.mean(pro_ms))
-    achieved_tflops = flop_per_launch / (attn_avg * 1e-3) / 1e12
+    achieved_tflops = flop_per_launch / (attn_avg * 1e-3) / 1e12 if attn_avg else 0.0
     peak = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
     # attention kernel bytes: read q, k, v (4096 + 2048 + 2048 B), write out (4096 B)
     attn_kernel_bytes = T * 12288
     ridge = peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
-    intensity = flop_per_launch / attn_kernel_bytes
+    intensity = flop_per_launch / attn_kernel_bytes if T else 0.0
     hbm_bound = intensity < ridge
     pro_bytes = T * (2048 + 1024) * 2 * 2  # read q,k columns; write q,k
     attn_bytes = T * 12288  # algorithmic bytes of the hot path per token
-    traffic = None
+    traffic, traffic_src = None, None
     tfile = os.path.join(ROOT, "profiles", "attention_traffic.json")
     if os.path.exists(tfile):
         with open(tfile) as f:
             tinfo = json.load(f).get(w.name)
         if tinfo:
-            traffic = tinfo["bytes_per_launch"]
+            # DRAM traffic grows with the tokens of a launch (requests of one
+            # length), so a capture is scaled to this rank's share
+            traffic = tinfo["bytes_per_launch"] * T / plan.total_tokens
+            traffic_src = ("not measured by this run: scaled from a smaller ncu capture ("
+                           + tinfo["source"] + ")")
+    ms_safe = ms if ms > 0 else float("nan")
+    strong = not args.weak_scaling
     line = {
-        "metric": METRIC, "value": world * T / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "metric": METRIC, "value": T_all / (ms_safe / 1e3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "higher_is_better": True, "scaling": "strong" if strong else "weak",
+        "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded N(0,1) qkv per layer, weights 1+N(0,0.02))",
-        "config": {"workload": w.name, "requests_per_rank": len(w.lengths),
-                   "seq_len": int(max(w.lengths)), "tokens_per_rank": T, "layers": L,
-                   "mode": ["auto(sparse<=8192)", "full", "sparse"][w.mode],
-                   "global_batch": world * len(w.lengths), "parallelism": f"dp{world} (by request)",
-                   "l2": "inputs larger than L2 (one 655 MB qkv per layer)"},
+        "config": {"workload": w.name, "requests": len(w.lengths) * (1 if strong else world),
+                   "seq_len": int(max(w.lengths)), "tokens": T_all, "layers": L,
+                   "mode": ["auto(sparse<=8192)", "full", "sparse"][w.mode]
+                           + (" -> sparse" if mode == 2 else " -> full"),
+                   "global_batch": len(w.lengths) * (1 if strong else world),
+                   "parallelism": (f"requests split over {world} GPU(s) (LPT on kept pairs), "
+                                   "host gather, no collective" if strong else
+                                   f"dp{world}: every rank runs the whole workload"),
+                   "requests_per_rank": ([len(r) for r in plan.assignment] if strong
+                                         else [len(w.lengths)] * world),
+                   "tokens_per_rank": ([plan.local_tokens(r) for r in range(world)] if strong
+                                       else [T] * world),
+                   "l2": "inputs larger than L2 (one qkv of >= 82 MB per layer per rank)"
+                         if T * 8192 > 126e6 else
+                         "qkv per layer smaller than L2; each of the 28 layers reads its own "
+                         "buffer, so the 28 x qkv working set exceeds L2"},
+        "rank_ms_per_step": rank_ms,
         "roofline": ({"bound": "hbm", "achieved": attn_kernel_bytes / (attn_avg * 1e-3) / 1e9,
                       "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": attn_kernel_bytes / (attn_avg * 1e-3) / 1e9 / peaks["hbm_gbs"],
@@ -671,32 +669,107 @@ def main():
                      if hbm_bound else
                      {"bound": "tensor", "achieved": achieved_tflops, "peak": peak,
                       "unit": "TFLOP/s", "frac": achieved_tflops / peak,
+                      "frac_burst": achieved_tflops / peaks["bf16_tflops"],
+                      "peak_burst": peaks["bf16_tflops"],
                       "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a "
-                                     f"{L}-layer step)"}),
+                                     f"{L}-layer step); frac_burst against {src} bf16_tflops"})
+                    if attn_avg else {"bound": None, "achieved": None, "note": "rank 0 idle"},
         "prologue": {"avg_launch_ms": pro_avg, "bytes_per_launch": pro_bytes,
-                     "achieved_gbs": pro_bytes / (pro_avg * 1e-3) / 1e9,
+                     "achieved_gbs": pro_bytes / (pro_avg * 1e-3) / 1e9 if pro_avg else None,
                      "peak_gbs": peaks["hbm_gbs"],
-                     "frac": pro_bytes / (pro_avg * 1e-3) / 1e9 / peaks["hbm_gbs"]},
-        "attention_share_of_step": float(np.sum(attn_ms) / args.steps / ms),
+                     "frac": pro_bytes / (pro_avg * 1e-3) / 1e9 / peaks["hbm_gbs"]
+                     if pro_avg else None},
+        "attention_share_of_step": float(np.sum(attn_ms) / args.steps / rank_ms[0])
+        if rank_ms[0] else None,
         "algorithmic_bytes_per_token_layer": 12288, "hot_path_bytes_per_step": attn_bytes * L,
-        "gpu_launches": 2 * L * args.steps,  # graph replays in the timed region
-        "timing": "CUDA graph of one step replayed K times; per-kernel times from an eager "
-                  "event-instrumented pass of the same K steps",
+        "gpu_launches": 0 if idle else 2 * L * args.steps,  # rank 0's launches in the region
+        "timing": "CUDA graph of one step replayed K times (max over ranks); per-kernel times "
+                  "(rank 0) from an eager event-instrumented pass of the same K steps",
         "clocks": clocks.summary(),
     }
-    line["roofline"].update({"traffic": traffic, "kernel": "attention_kernel",
-                             "flop_per_launch": flop_per_launch,
-                             "bytes_per_launch": attn_kernel_bytes,
-                             "arithmetic_intensity": intensity, "ridge": ridge,
-                             "avg_launch_ms": attn_avg})
+    if attn_avg:
+        line["roofline"].update({"traffic": traffic, "traffic_source": traffic_src,
+                                 "kernel": "attention_kernel",
+                                 "flop_per_launch": flop_per_launch,
+                                 "bytes_per_launch": attn_kernel_bytes,
+                                 "arithmetic_intensity": intensity, "ridge": ridge,
+                                 "avg_launch_ms": attn_avg})
     if e2e:
         line["e2e"] = e2e
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(pkg, w)
     print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def run_e2e(args, torch, ex, plan, me, world, rank, local, dev, layers, ctx, barrier, T, T_all,
+            L):
+    """The e2e leg (see main): returns the e2e dict (on every rank)."""
+    Tg = plan.total_tokens
+    shared = world > 1 and not args.weak_scaling
+    in_shape, out_shape = (Tg, 4096), (Tg, 16, 128)
+    nbytes = 2 * (Tg * 4096 * 2 + Tg * 2048 * 2)
+    bufs = None
+    gather = "one page-locked host buffer"
+    if shared:
+        if ex.SharedHostBuffer.fits(nbytes):
+            tag = os.environ.get("MASTER_PORT", "0")
+            names = [f"/dev/shm/qwa_bench_{tag}_{n}" for n in ("in0", "in1", "out0", "out1")]
+            shapes = [in_shape, in_shape, out_shape, out_shape]
+            if rank == 0:
+                bufs = [ex.SharedHostBuffer(n, sh, create=True) for n, sh in zip(names, shapes)]
+            barrier()
+            if rank != 0:
+                bufs = [ex.SharedHostBuffer(n, sh) for n, sh in zip(names, shapes)]
+            host_in = [b.tensor for b in bufs[:2]]
+            host_out = [b.tensor for b in bufs[2:]]
+            gather = ("host buffers in shared memory mapped by every rank: each rank copies its "
+                      "requests' output rows to their place")
+        else:
+            shared = False
+            gather = "per-rank page-locked buffers (shared memory too small for the gather)"
+    if not shared:
+        host_in = [torch.empty(in_shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+        host_out = [torch.empty(out_shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    # each rank writes its own requests' rows of the host input
+    ranges = plan.row_ranges(me)
+    for h in host_in:
+        for g, l0, n in ranges:
+            h[g:g + n].copy_(layers[0][0][l0:l0 + n])
+    barrier()
+    backend = ex.DeviceBackend(local, T, buffers=2, ctx=ctx)
+    shard = ex.ShardExecutor(plan, me, backend)
+    ins = [host_in[l % 2] for l in range(L)]
+    outs = [host_out[l % 2] for l in range(L)]
+    ws = [(qw, kw) for _, qw, kw in layers]
+    shard.run(ins, outs, ws)
+    torch.cuda.synchronize()
+    backend.check()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(backend.stream)
+    for _ in range(args.e2e_steps):
+        shard.run(ins, outs, ws)
+    e1.record(backend.stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps if T else 0.0
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    if bufs:
+        barrier()
+        for b in bufs:
+            b.close(unlink=rank == 0)
+    return {"value": T_all / (e2e_ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": T * 4096 * 2 * L, "d2h_bytes_per_step": T * 2048 * 2 * L,
+            "bytes_scope": "per rank (rank 0)" if world > 1 else "whole job",
+            "ms_per_step": e2e_ms, "gather": gather,
+            "path": "executor.ShardExecutor + DeviceBackend (qwa_prefill_attention_layer)"}
 
 
 if __name__ == "__main__":

@@ -257,8 +257,9 @@ def prefill_attention_layer(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight:
                             cu_seqlens: Sequence[int], mode: int = MODE_AUTO,
                             prefix: int = PREFIX, window: int = WINDOW, eps: float = EPSILON,
                             theta: float = ROPE_THETA, q_buf=None, k_buf=None, out=None,
-                            stream=None) -> torch.Tensor:
-    """Prologue + attention of one layer (model.ts:94-95): qkv [T, 4096] f16."""
+                            stream=None, ctx: Optional[Context] = None) -> torch.Tensor:
+    """Prologue + attention of one layer (model.ts:94-95): qkv [T, 4096] f16.
+    ``ctx``: the context to launch on (default: the device's shared one)."""
     _f16_cuda(qkv, "qkv")
     _f32_weight(q_weight, "q_weight")
     _f32_weight(k_weight, "k_weight")
@@ -270,7 +271,7 @@ def prefill_attention_layer(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight:
                                                         device=dev)
     out = out if out is not None else torch.empty(T, Q_HEADS, HEAD_DIM, dtype=torch.float16,
                                                   device=dev)
-    ctx = Context.for_device(dev.index)
+    ctx = ctx if ctx is not None else Context.for_device(dev.index)
     cu = _lib.cu_array(cu_seqlens)
     st = ctx.lib.qwa_prefill_attention_layer(ctx.handle, _ptr(qkv), qkv.shape[1], _ptr(q_weight),
                                              _ptr(k_weight), _ptr(q_buf), _ptr(k_buf), _ptr(out),

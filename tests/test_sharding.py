@@ -33,6 +33,28 @@ def test_gather_order_restores_batch(pkg):
     assert [flat[j] for j in order] == [0, 1, 2, 3, 4]
 
 
+def test_shard_plan_rows_and_mode(pkg):
+    ex = pkg.executor
+    plan = ex.ShardPlan([7, 40, 0, 3, 25, 12], 3, mode=0)
+    rows = []
+    for r in range(3):
+        local = 0
+        for g, l0, n in plan.row_ranges(r):
+            assert l0 == local
+            rows.extend(range(g, g + n))
+            local += n
+        assert local == plan.local_tokens(r)
+    assert sorted(rows) == list(range(plan.total_tokens))
+    # one rank holds every request: its rows form a single run
+    assert ex.ShardPlan([5, 6, 7], 1).row_ranges(0) == [(0, 0, 18)]
+    # AUTO is resolved on the whole batch: a rank holding only a short request
+    # still runs full causal when another request exceeds 8192 tokens
+    p = ex.ShardPlan([9000, 20], 2, mode=0)
+    assert p.resolved_mode == ex.MODE_FULL
+    assert ex.ShardPlan([8192, 20], 2).resolved_mode == ex.MODE_SPARSE
+    assert ex.ShardPlan([20], 4).local_tokens(3) == 0
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -41,43 +63,83 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, result_path):
+class _OracleBackend:
+    """The CPU oracle in place of the device, for the executor's host logic."""
+    buffers = 1
+
+    def __init__(self, oracle, tokens):
+        self.o = oracle
+        self.x = np.zeros((tokens, 4096), np.float16)
+        self.out = None
+
+    def stage_in(self, b, ranges, host):
+        for g, l0, n in ranges:
+            self.x[l0:l0 + n] = host[g:g + n]
+
+    def compute(self, b, cu, weights, mode, prefix, window):
+        q, k = self.o.c_qk_norm_rope(self.x, weights[0], weights[1], cu)
+        self.out = self.o.c_attention(q.astype(np.float16), k.astype(np.float16), self.x, 4096,
+                                      3072, cu, mode, prefix, window).astype(np.float16)
+
+    def stage_out(self, b, ranges, host):
+        for g, l0, n in ranges:
+            host[g:g + n] = self.out[l0:l0 + n]
+
+    def finish(self):
+        return None
+
+
+LENGTHS, LAYERS = [7, 40, 3, 0, 25, 12], 2
+
+
+def _rank_main(rank, world, port, tmp):
     import importlib
     import sys
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
     from oracle import oracle
     pkg = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200")
+    ex = pkg.executor
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    lengths = [7, 40, 3, 25, 12]
-    mode, prefix, window = 2, 5, 11
-    rng = np.random.default_rng(99)  # same batch on every rank
-    cu = [0] + list(np.cumsum(lengths))
-    qkv = rng.standard_normal((cu[-1], 4096)).astype(np.float16)
-    assignment = pkg.sharding.lpt_shard(lengths, world, mode)
-    mine = assignment[rank]
-    # each rank computes only its requests (here with the oracle standing in
-    # for the device) and the host gathers per-rank outputs
-    sub_cu = [0] + list(np.cumsum([lengths[i] for i in mine]))
-    rows = np.concatenate([np.arange(cu[i], cu[i + 1]) for i in mine]) if mine else np.zeros(0, int)
-    q = qkv[rows, :2048].reshape(-1, 16, 128).copy()
-    k = qkv[rows, 2048:3072].reshape(-1, 8, 128).copy()
-    out = oracle.c_attention(q, k, qkv[rows].copy(), 4096, 3072, sub_cu, mode, prefix, window)
-    per_req = [out[sub_cu[n]:sub_cu[n + 1]] for n in range(len(mine))]
-    gathered = [None] * world
-    dist.all_gather_object(gathered, per_req)
+    plan = ex.ShardPlan(LENGTHS, world, mode=2)
+    T = plan.total_tokens
+    # host buffers shared by the ranks: rank 0 creates them, the others map them
+    names = [f"{tmp}/in{l}" for l in range(LAYERS)] + [f"{tmp}/out{l}" for l in range(LAYERS)]
+    shapes = [(T, 4096)] * LAYERS + [(T, 16, 128)] * LAYERS
     if rank == 0:
-        flat = [r for part in gathered for r in part]
-        order = pkg.sharding.gather_order(assignment)
-        full = np.concatenate([flat[j] for j in order])
-        ref = oracle.c_attention(qkv[:, :2048].reshape(-1, 16, 128).copy(),
-                                 qkv[:, 2048:3072].reshape(-1, 8, 128).copy(), qkv, 4096, 3072,
-                                 cu, mode, prefix, window)
-        np.save(result_path, np.abs(full - ref).max())
+        bufs = [ex.SharedHostBuffer(n, s, create=True, pin=False) for n, s in zip(names, shapes)]
+        rng = np.random.default_rng(99)
+        for l in range(LAYERS):
+            bufs[l].array[:] = rng.standard_normal((T, 4096)).astype(np.float16)
+        dist.barrier()
+    else:
+        dist.barrier()
+        bufs = [ex.SharedHostBuffer(n, s, pin=False) for n, s in zip(names, shapes)]
+    wrng = np.random.default_rng(5)
+    weights = [tuple((1 + 0.02 * wrng.standard_normal(128)).astype(np.float32) for _ in range(2))
+               for _ in range(LAYERS)]
+    # assign -> compute (oracle in place of the device) -> gather into the
+    # shared host output at each request's rows
+    executor = ex.ShardExecutor(plan, rank, _OracleBackend(oracle, plan.local_tokens(rank)),
+                                prefix=5, window=11)
+    executor.run([b.array for b in bufs[:LAYERS]], [b.array for b in bufs[LAYERS:]], weights)
+    dist.barrier()
+    if rank == 0:
+        errs = []
+        for l in range(LAYERS):
+            x = bufs[l].array
+            q, k = oracle.c_qk_norm_rope(x, weights[l][0], weights[l][1], plan.cu)
+            ref = oracle.c_attention(q.astype(np.float16), k.astype(np.float16), x, 4096, 3072,
+                                     plan.cu, 2, 5, 11).astype(np.float16)
+            errs.append(float(np.abs(bufs[LAYERS + l].array.astype(np.float64) - ref).max()))
+        np.save(f"{tmp}/err.npy", np.array(errs))
+    dist.barrier()
+    for b in bufs:
+        b.close()
     dist.destroy_process_group()
 
 
-def test_two_rank_shard_and_host_gather(tmp_path, pkg):
-    path = str(tmp_path / "err.npy")
-    mp.spawn(_rank_main, args=(2, _free_port(), path), nprocs=2, join=True)
-    assert float(np.load(path)) < 1e-12
+def test_two_rank_executor_shards_and_gathers(tmp_path, pkg):
+    mp.spawn(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    errs = np.load(str(tmp_path / "err.npy"))
+    assert errs.shape == (LAYERS,) and float(errs.max()) == 0.0
