@@ -363,3 +363,135 @@ void oracle_rms_norm(uint16_t *x, const uint16_t *residual, const float *weight,
       nr[i] = float_to_half_rne((float)half_to_double(xr[i]) * inv * weight[i]);
   }
 }
+
+/* ------------------------------------------------------------------------
+ * "WGSL-faithful" mode: the reference's own arithmetic, not the exact math.
+ *
+ * Emulates tiledFlashAttentionShader (src/webgpu/ops.ts:168-241) with its
+ * rounding points, for one padded request of `S` rows (S <= 8192, the tiled
+ * path of ops.ts:328): 16-row query tiles x 16-key blocks, the block-skip
+ * test (:209), the keep test (:220), f16 dot products summed in f32 (:221),
+ * the f32 scale (:222), update_stats (:186-193: f32 block max and exps, f16
+ * weights, alphas, betas and running denominator), the f16 P.V and output
+ * accumulators (:227-232) and the f16 division (:238).
+ *
+ * WGSL leaves two things to the implementation, so they are parameters:
+ *   fused = 1: a*b + c in f16 is one rounding (an FMA, as GPU compilers
+ *              usually contract it); 0: product and sum rounded separately.
+ *   exp: C's expf (the shader's f32 exp has implementation-defined ulp
+ *        error; both are close to the exact exponential).
+ * The f16 dot(vec4, vec4) is an FMA chain over the four lanes (one rounding
+ * per lane with fused = 1, two without).
+ * ------------------------------------------------------------------------ */
+
+/* double -> nearest f16 value (ties to even), as a double; +-inf past 65504 */
+static double rf16(double x) {
+  if (x == 0.0 || isnan(x) || isinf(x)) return x;
+  int e;
+  frexp(x, &e);
+  int lead = e - 1;
+  if (lead < -14) lead = -14; /* subnormal spacing 2^-24 */
+  const double step = ldexp(1.0, lead - 10);
+  const double r = nearbyint(x / step) * step;
+  if (fabs(r) > 65504.0) return copysign(INFINITY, x);
+  return r;
+}
+
+static double f16_fma(double a, double b, double c, int fused) {
+  return fused ? rf16(a * b + c) : rf16(rf16(a * b) + c);
+}
+
+/* q: [T,16,128] f16, k: [T,8,128] f16, v at v[t*v_stride + v_offset + g*128],
+ * requests of cu (each its own padded sequence), out: [T,16,128] as the f16
+ * values the shader would write (in doubles). */
+void oracle_attention_wgsl(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                           int64_t v_stride, int64_t v_offset, const int32_t *cu, int batch,
+                           int fused, double *out) {
+  init_lut();
+  int64_t n_units = 0; /* (request, head, 16-row tile) */
+  for (int b = 0; b < batch; ++b) n_units += (int64_t)((cu[b + 1] - cu[b] + 15) / 16) * 16;
+  const float scale = 0.08838834764831845f;
+  const float lowest = -3.402823e38f;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int64_t u = 0; u < n_units; ++u) {
+    int b = 0;
+    int64_t acc = 0;
+    for (;; ++b) {
+      const int64_t n = (int64_t)((cu[b + 1] - cu[b] + 15) / 16) * 16;
+      if (u < acc + n) break;
+      acc += n;
+    }
+    const int64_t local = u - acc;
+    const int head = (int)(local % 16), gx = (int)(local / 16), kv = head / 2;
+    const int S = cu[b + 1] - cu[b];
+    const int64_t base = cu[b];
+    float maxima[16];
+    double den[16], total[16][128], weights[16][16], alpha16[16], beta16[16];
+    for (int r = 0; r < 16; ++r) {
+      maxima[r] = lowest;
+      den[r] = 0.0;
+      for (int d = 0; d < 128; ++d) total[r][d] = 0.0;
+    }
+    const int key_limit = S < (gx + 1) * 16 ? S : (gx + 1) * 16;
+    const int prefix_size = S < 176 ? S : 176, local_window = S < 432 ? S : 432;
+    const int qts = gx * 16;
+    const int local_start = qts + 1 > local_window ? qts + 1 - local_window : 0;
+    for (int kb = 0; kb < key_limit; kb += 16) {
+      if (kb >= prefix_size && kb + 15 < local_start) continue;
+      for (int r = 0; r < 16; ++r) {
+        const int qp = qts + r;
+        float sc[16];
+        for (int c = 0; c < 16; ++c) {
+          const int kp = kb + c;
+          float s = lowest;
+          if (qp < S && kp <= qp && kp < S && (kp < prefix_size || kp + local_window > qp)) {
+            s = 0.f;
+            const uint16_t *qr = q + ((base + qp) * 16 + head) * 128;
+            const uint16_t *kr = k + ((base + kp) * 8 + kv) * 128;
+            for (int d4 = 0; d4 < 32; ++d4) {
+              double dv = rf16(H2D(qr[4 * d4]) * H2D(kr[4 * d4]));
+              for (int i = 1; i < 4; ++i)
+                dv = f16_fma(H2D(qr[4 * d4 + i]), H2D(kr[4 * d4 + i]), dv, fused);
+              s += (float)dv;
+            }
+            s *= scale;
+          }
+          sc[c] = s;
+        }
+        /* update_stats (ops.ts:186-193) */
+        float block_max = lowest;
+        for (int c = 0; c < 16; ++c) block_max = fmaxf(block_max, sc[c]);
+        float block_den = 0.f;
+        for (int c = 0; c < 16; ++c) {
+          const float w = expf(sc[c] - block_max);
+          weights[r][c] = rf16(w);
+          block_den += w;
+        }
+        const float next_max = fmaxf(maxima[r], block_max);
+        const float alpha = expf(maxima[r] - next_max), beta = expf(block_max - next_max);
+        alpha16[r] = rf16(alpha);
+        beta16[r] = rf16(beta);
+        den[r] = f16_fma(den[r], alpha16[r], rf16(beta * block_den), fused);
+        maxima[r] = next_max;
+      }
+      /* P.V in f16 and the rescaled running output (ops.ts:227-232) */
+      for (int r = 0; r < 16; ++r)
+        for (int d = 0; d < 128; ++d) {
+          double av = 0.0;
+          for (int c = 0; c < 16; ++c) {
+            const int kp = kb + c;
+            const double vv =
+                kp < S ? H2D(v[(base + kp) * v_stride + v_offset + kv * 128 + d]) : 0.0;
+            av = f16_fma(weights[r][c], vv, av, fused);
+          }
+          total[r][d] = f16_fma(total[r][d], alpha16[r], rf16(beta16[r] * av), fused);
+        }
+    }
+    for (int r = 0; r < 16; ++r) {
+      const int qp = qts + r;
+      if (qp >= S) continue;
+      for (int d = 0; d < 128; ++d)
+        out[((base + qp) * 16 + head) * 128 + d] = rf16(total[r][d] / den[r]);
+    }
+  }
+}

@@ -75,6 +75,8 @@ def lib():
         L.oracle_float_to_half_rne.argtypes = [ctypes.c_float]
         L.oracle_rms_norm.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                       ctypes.c_int]
+        L.oracle_attention_wgsl.argtypes = [P, P, P, ctypes.c_int64, ctypes.c_int64, P,
+                                            ctypes.c_int, ctypes.c_int, P]
         L.oracle_threads.restype = ctypes.c_int
         L.oracle_set_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -146,6 +148,27 @@ def c_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, v_stride: int, v_of
     if T:
         lib().oracle_attention(_ptr(q), _ptr(k), _ptr(v), v_stride, v_offset, _ptr(cu),
                                len(cu) - 1, mode, prefix, window, _ptr(out))
+    return out
+
+
+def c_attention_wgsl(q: np.ndarray, k: np.ndarray, v: np.ndarray, v_stride: int, v_offset: int,
+                     cu_seqlens, fused: bool = True) -> np.ndarray:
+    """The reference shader's own arithmetic (src/webgpu/ops.ts:168-241): f16
+    dot products, f16 weights / denominators / accumulators, 16-key blocks,
+    each request its own padded sequence (tiled path, S <= 8192). Returns the
+    f16 values it would write, as fp64 [T,16,128]. ``fused``: f16 a*b+c
+    rounded once (FMA contraction) or twice."""
+    q = np.ascontiguousarray(q, dtype=np.float16)
+    k = np.ascontiguousarray(k, dtype=np.float16)
+    v = np.ascontiguousarray(v, dtype=np.float16)
+    assert v.shape[-1] == v_stride
+    cu = _cu(cu_seqlens)
+    assert int(np.max(np.diff(cu), initial=0)) <= 8192, "tiled path only (S <= 8192)"
+    T = int(cu[-1])
+    out = np.zeros((T, Q_HEADS, HEAD_DIM), dtype=np.float64)
+    if T:
+        lib().oracle_attention_wgsl(_ptr(q), _ptr(k), _ptr(v), v_stride, v_offset, _ptr(cu),
+                                    len(cu) - 1, 1 if fused else 0, _ptr(out))
     return out
 
 

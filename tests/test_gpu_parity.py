@@ -244,6 +244,13 @@ def test_full_size_config5_sampled_rows(pkg, oracle, cuda_dev, mode):
     got = out.view(T * 16, 128)[torch.from_numpy(rows).cuda()].cpu().numpy().astype(np.float64)
     err = np.abs(got - ref).max()
     assert err <= MAX_ABS, err
+    # cosine per head over the sampled rows of that head
+    for h in range(16):
+        sel = rows % 16 == h
+        if sel.any():
+            a, b = got[sel].ravel(), ref[sel].ravel()
+            cos = a @ b / (np.linalg.norm(a) * np.linalg.norm(b))
+            assert cos >= MIN_COS, f"head {h}: cosine {cos}"
     # linearity in V and the constant-V property on every row
     v2 = torch.randn(T, 1024, generator=g, device="cuda").half() * 0.5
     out2 = attn.attention(q, k, v2, cu, 1024, 0, mode)
@@ -286,3 +293,47 @@ def test_invalid_arguments_raise(pkg, cuda_dev):
     assert e.value.status == attn._lib.QWA_ERR_UNSUPPORTED
     with pytest.raises(ValueError):
         attn.attention(q.float(), k, v, [0, 64])
+
+
+@pytest.mark.parametrize("name,lengths", [
+    ("c1_single_50", [50]),
+    ("c2_ragged16", None),
+    ("c3_16x500 (4 of the 16 requests)", [500] * 4),
+])
+def test_distance_to_the_reference_arithmetic(pkg, oracle, cuda_dev, name, lengths):
+    """How far the GPU output sits from the reference shader's own arithmetic
+    (f16 weights, denominators and accumulators; the oracle's WGSL mode) and
+    from the exact math. The GPU path computes in fp32 and is the closer of
+    the two to the exact result; both stay within f16 accumulation error of
+    each other. Prints one line per case for the record."""
+    if lengths is None:
+        lengths = list(pkg.workloads.WORKLOADS["c2_ragged16"].lengths)
+    cu, qkv, qw, kw = _random_case(lengths, 17)
+    attn = pkg.attention
+    q, k = attn.qk_norm_rope(_dev(qkv), _dev(qw), _dev(kw), cu)
+    out = attn.attention(q, k, _dev(qkv), cu, 4096, 3072)
+    attn.Context.for_device(0).check()
+    q16, k16 = q.cpu().numpy(), k.cpu().numpy()
+    got = out.cpu().numpy().astype(np.float64)
+    exact = oracle.c_attention(q16, k16, qkv, 4096, 3072, cu)
+    line = {"case": name}
+    for fused in (True, False):
+        ref_arith = oracle.c_attention_wgsl(q16, k16, qkv, 4096, 3072, cu, fused)
+        tag = "fma" if fused else "unfused"
+
+        def min_cos(a, b):
+            a, b = a.reshape(-1, 128), b.reshape(-1, 128)
+            return float(((a * b).sum(1) / np.linalg.norm(a, axis=1)
+                          / np.linalg.norm(b, axis=1)).min())
+        line[f"gpu_vs_wgsl_{tag}_maxabs"] = float(np.abs(got - ref_arith).max())
+        line[f"gpu_vs_wgsl_{tag}_min_row_cos"] = min_cos(got, ref_arith)
+        line[f"wgsl_{tag}_vs_exact_maxabs"] = float(np.abs(ref_arith - exact).max())
+        assert line[f"gpu_vs_wgsl_{tag}_min_row_cos"] >= 0.999
+        assert np.abs(got - exact).max() <= np.abs(ref_arith - exact).max()
+    line["gpu_vs_exact_maxabs"] = float(np.abs(got - exact).max())
+    line["gpu_vs_exact_min_row_cos"] = float(
+        ((got.reshape(-1, 128) * exact.reshape(-1, 128)).sum(1)
+         / np.linalg.norm(got.reshape(-1, 128), axis=1)
+         / np.linalg.norm(exact.reshape(-1, 128), axis=1)).min())
+    print("REFERENCE_ARITHMETIC", line)
+    assert line["gpu_vs_exact_maxabs"] <= MAX_ABS

@@ -160,3 +160,47 @@ def test_rms_norm_c_matches_numpy(oracle, has_residual):
     # RMS of the normalized row (before the weight) is 1
     rms = np.sqrt(np.mean((cn.astype(np.float64) / w) ** 2, axis=1))
     assert np.allclose(rms, 1.0, atol=2e-3)
+
+
+def _qkv(rng, lengths):
+    cu = [0] + list(np.cumsum(lengths))
+    T = cu[-1]
+    q = rng.standard_normal((T, 16, 128)).astype(np.float16)
+    k = rng.standard_normal((T, 8, 128)).astype(np.float16)
+    v = rng.standard_normal((T, 1024)).astype(np.float16)
+    return cu, q, k, v
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_wgsl_mode_known_answers(oracle, fused):
+    """The reference-arithmetic emulation (ops.ts:168-241 with its f16 rounding
+    points): a one-token request returns its value row exactly; identical keys
+    give the f16 mean of the kept values."""
+    rng = np.random.default_rng(8)
+    cu, q, k, v = _qkv(rng, [1, 40])
+    out = oracle.c_attention_wgsl(q, k, v, 1024, 0, cu, fused)
+    for h in range(16):
+        assert np.array_equal(out[0, h], v[0, (h // 2) * 128:(h // 2 + 1) * 128].astype(np.float64))
+    k[:] = k[0]
+    out = oracle.c_attention_wgsl(q, k, v, 1024, 0, cu, fused)
+    v2 = v[1:].astype(np.float64).reshape(40, 8, 128)
+    for t in range(40):
+        mean = v2[:t + 1].mean(0)
+        for h in range(16):
+            # f16 running sums of up to 40 values near N(0, 1)
+            assert np.abs(out[1 + t, h] - mean[h // 2]).max() < 8e-3
+
+
+@pytest.mark.parametrize("lengths", [[50], [16, 33, 130], [700]])
+def test_wgsl_mode_is_close_to_exact_math(oracle, lengths):
+    """The emulated reference stays within f16 accumulation error of the exact
+    attention, including the sparse rule (700 > 608) and the block skip."""
+    rng = np.random.default_rng(len(lengths))
+    cu, q, k, v = _qkv(rng, lengths)
+    ex = oracle.c_attention(q, k, v, 1024, 0, cu)
+    for fused in (True, False):
+        w = oracle.c_attention_wgsl(q, k, v, 1024, 0, cu, fused)
+        assert np.abs(w - ex).max() < 1e-2
+        a, b = w.reshape(-1, 128), ex.reshape(-1, 128)
+        cos = (a * b).sum(1) / np.linalg.norm(a, axis=1) / np.linalg.norm(b, axis=1)
+        assert cos.min() > 0.999
