@@ -132,8 +132,21 @@ QWA_API qwa_status qwa_prefill_attention_layer(qwa_ctx *ctx, const void *qkv, in
 
 /* Synchronise `stream` and report any device-side error recorded by the
  * kernels since the last check (e.g. QWA_ERR_TIMEOUT from a bounded wait);
- * clears the recorded error. */
+ * clears the recorded error. ctx == NULL checks the status word of
+ * qwa_attention_noalloc on the current device instead (no allocation). */
 QWA_API qwa_status qwa_check(qwa_ctx *ctx, void *stream);
+
+/* Bounded waits and their test hook. Every wait of the attention kernel on
+ * one of its pipeline barriers gives up after wait_limit_ns (<= 0: the
+ * default, 2 s), makes the whole CTA stop, lets the copies and MMAs it has
+ * already issued complete, frees its tensor memory and records
+ * QWA_ERR_TIMEOUT for qwa_check; the context stays usable. skip_kv_load >= 0
+ * makes the first CTA of every later attention call on this context leave
+ * out its K/V load number skip_kv_load, so a wait runs out (used by the
+ * tests to exercise that path); -1 turns it off. No counterpart in the
+ * reference, whose shaders have no error reporting (a failed batch is
+ * rejected whole by the engine, src/webgpu/embedding-engine.ts:76-81). */
+QWA_API qwa_status qwa_set_debug(qwa_ctx *ctx, int64_t wait_limit_ns, int skip_kv_load);
 
 /* Algorithmic work of an attention call: kept (q,k) pairs summed over the
  * batch (per q-head; FLOPs = 8192 * pairs), and key tiles the kernel visits. */
@@ -154,12 +167,15 @@ QWA_API qwa_status qwa_selftest_tile(qwa_ctx *ctx, const void *a, const void *b,
  * arena; processes that hold no qwa_ctx). No counterpart in the reference.
  * Same arguments and results as qwa_attention, on the current device, but the
  * work list and status word live in a fixed 1 MiB device array owned by the
- * library (held by every GPU that loads it until exit): a call needing more
- * than 65,520 work items -- ceil(len/128) * 8 summed over requests, about one
- * million tokens -- returns QWA_ERR_INVALID_ARG without launching. The first
- * call on each device looks up that array's address; make it before any
- * stream capture. All calls share the array: calls that overlap on the GPU
- * race. Device-side timeouts are recorded in that array, not reported. */
+ * library (held by every GPU that loads it until exit). The work list is
+ * built on the device from cu_seqlens passed in the launch's parameters, so
+ * the call enqueues no host-to-device copy. Limits: at most 4096 requests
+ * and 65,520 work items -- ceil(len/128) * 8 summed over requests, about one
+ * million tokens; a larger call returns QWA_ERR_INVALID_ARG without
+ * launching. The first call on each device looks up that array's address;
+ * make it before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race. A device-side timeout is recorded in the array and
+ * reported by qwa_check(NULL, stream). */
 QWA_API qwa_status qwa_attention_noalloc(const void *q, const void *k, const void *v,
                                          int64_t v_stride, int64_t v_offset, void *out,
                                          const int32_t *cu_seqlens_host, int batch, int mode,

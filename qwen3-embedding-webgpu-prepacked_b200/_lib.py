@@ -34,6 +34,7 @@ SIGNATURES = {
     "qwa_prefill_attention_layer": (I32, [P, P, I64, P, P, P, P, P, I32P, I32, I32, I32, I32, F32,
                                           F32, P]),
     "qwa_check": (I32, [P, P]),
+    "qwa_set_debug": (I32, [P, I64, I32]),
     "qwa_attention_work": (I32, [I32P, I32, I32, I32, I32, I64P, I64P]),
     "qwa_selftest_tile": (I32, [P, P, P, P, P, P, P]),
     "qwa_attention_noalloc": (I32, [P, P, P, I64, I64, P, I32P, I32, I32, I32, I32, P]),

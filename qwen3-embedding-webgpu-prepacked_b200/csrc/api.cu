@@ -30,8 +30,6 @@ using namespace qwa;
 
 namespace {
 
-constexpr int kSparseMaxSeq = 8192;  // src/webgpu/ops.ts:328
-constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128), ops.ts:224
 constexpr size_t kMaxPlans = 64;
 
 struct Plan {
@@ -64,6 +62,8 @@ struct qwa_ctx {
   std::map<std::tuple<const void*, int, int>, __half*> weights;
   std::vector<__half*> retired;  // forgotten copies, freed outside stream capture
   unsigned long long* trace = nullptr;           // QWA_TRACE builds only
+  unsigned long long wait_ns = kWaitTimeoutNs;    // bounded-wait limit of the attention kernel
+  int skip_load = -1;                             // test hook, see qwa_set_debug
 };
 
 namespace {
@@ -179,12 +179,6 @@ qwa_status check_cu(qwa_ctx* ctx, const int32_t* cu, int batch, int* total, int*
   *total = cu[batch];
   *max_len = ml;
   return QWA_OK;
-}
-
-int resolve_sparse(int mode, int max_len) {
-  if (mode == QWA_MODE_FULL) return 0;
-  if (mode == QWA_MODE_SPARSE) return 1;
-  return max_len <= kSparseMaxSeq ? 1 : 0;
 }
 
 // Plan lookup/creation. sparse < 0 requests a plan without attention items
@@ -350,9 +344,11 @@ qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void*
   args.sparse = sparse;
   args.prefix = prefix;
   args.window = window;
-  args.scale_log2 = kScale * 1.4426950408889634f;
+  args.scale_log2 = kScale * kLog2e;
   args.status = ctx->d_status;
   args.trace = ctx->trace;
+  args.wait_ns = ctx->wait_ns;
+  args.skip_load = ctx->skip_load;
   QWA_CUDA(ctx, launch_attention(tm_q, tm_k, tm_v, tm_o, args, plan->n_items, stream));
   return QWA_OK;
 }
@@ -416,8 +412,19 @@ qwa_status qwa_destroy(qwa_ctx* ctx) {
   return QWA_OK;
 }
 
+qwa_status qwa_set_debug(qwa_ctx* ctx, int64_t wait_limit_ns, int skip_kv_load) {
+  if (!ctx || skip_kv_load < -1) return QWA_ERR_INVALID_ARG;
+  ctx->wait_ns = wait_limit_ns > 0 ? static_cast<unsigned long long>(wait_limit_ns)
+                                   : kWaitTimeoutNs;
+  ctx->skip_load = skip_kv_load;
+  return QWA_OK;
+}
+
+// status word of qwa_attention_noalloc on the current device (noalloc.cu)
+qwa_status qwa_noalloc_status(void* stream);
+
 qwa_status qwa_check(qwa_ctx* ctx, void* stream) {
-  if (!ctx) return QWA_ERR_INVALID_ARG;
+  if (!ctx) return qwa_noalloc_status(stream);
   DeviceGuard guard(ctx->device);
   QWA_CUDA(ctx, cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
   int code = 0;

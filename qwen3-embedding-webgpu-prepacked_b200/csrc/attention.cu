@@ -9,7 +9,7 @@
 // two MMA streams (GQA 2:1).
 //
 // Warp roles (320 threads):
-//   warp 0      TMA producer: Q tiles once, then K_j / V_j into a 4-slot ring
+//   warp 0      TMA producer: Q tiles once, then K_j / V_j into a 3-slot ring
 //   warp 1      TMEM owner; lane 0 issues every tcgen05.mma and commit
 //   warps 2-5   softmax warpgroup A (head 2g):   one thread per query row
 //   warps 6-9   softmax warpgroup B (head 2g+1)
@@ -77,11 +77,14 @@ enum Bar : int {
   kPHi = kPLo + 2,                   // +X: P of keys 64..127 in TMEM
   kOFinal = kPHi + 2,              // +X: O_X of the item complete
   kOStaged = kOFinal + 2,            // +X: O tile of head X staged in shared memory
-  kNumBars = kOStaged + 2
+  kDrain = kOStaged + 2,             // the issuer's MMAs all complete (at exit)
+  kNumBars = kDrain + 1
 };
 constexpr uint32_t kHolderOff = kBarOff + 8 * kNumBars;
 constexpr uint32_t kAbortOff = kHolderOff + 4;
-constexpr uint32_t kSmemUsed = kAbortOff + 4;
+constexpr uint32_t kLimitOff = kHolderOff + 8;  // bounded-wait limit (ns), 8-byte aligned
+static_assert(kLimitOff % 8 == 0, "limit alignment");
+constexpr uint32_t kSmemUsed = kLimitOff + 8;
 constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
@@ -97,6 +100,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = smem_addr(smem);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + kHolderOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kAbortOff);
+  volatile unsigned long long* wait_limit =
+      reinterpret_cast<volatile unsigned long long*>(smem + kLimitOff);
   auto bar = [&](int i) -> uint32_t { return sbase + kBarOff + 8u * i; };
 
   const int warp = threadIdx.x >> 5;
@@ -119,7 +124,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int x = 0; x < 2; ++x) mbar_init(bar(kOFinal + x), 1);
     for (int x = 0; x < 2; ++x) mbar_init(bar(kOStaged + x), 4);  // one arrival per warp
+    mbar_init(bar(kDrain), 1);
     *abort_flag = 0;
+    *wait_limit = args.wait_ns;
     fence_mbar_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
@@ -144,6 +151,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int c = 0;  // K/V ring uses
       bool ok = true;
+      // last full phase issued per K/V slot (bits 0-2) and Q buffer (bits
+      // 3-4): bit i+8 set once one was issued, bit i its parity. Waited for
+      // before exit so no copy lands after it.
+      uint32_t issued = 0;
       AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
       for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
         // the next item's descriptor is loaded one item ahead (a global load
@@ -154,9 +165,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
         const int qb = li & 1;
         if (!(ok = mbar_wait(bar(kQEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, args.status,
-                             kDevTimeoutQ)))
+                             kDevTimeoutQ, wait_limit)))
           break;
         mbar_arrive_expect_tx(bar(kQFull + qb), kQBufBytes);
+        issued = (issued & ~(1u << (kSlots + qb))) | (1u << (kSlots + qb + 8)) |
+                 (static_cast<uint32_t>((li >> 1) & 1) << (kSlots + qb));
         for (int x = 0; x < 2; ++x) {
           const uint32_t dst = sbase + kQOff + qb * kQBufBytes + x * kTileBytes;
           tma_load_3d(dst, &tm_q, bar(kQFull + qb), 0, 2 * g + x, row0);
@@ -167,17 +180,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kv = 0; kv < 2; ++kv, ++c) {
             const int s = c % kSlots;
             if (!(ok = mbar_wait(bar(kSlotEmpty + s), ((c / kSlots) & 1) ^ 1, abort_flag,
-                                 args.status, kDevTimeoutSlotEmpty)))
+                                 args.status, kDevTimeoutSlotEmpty, wait_limit)))
               break;
+            // test hook (qwa_set_debug): CTA 0 leaves one load out, so the
+            // MMA issuer's bounded wait for it runs out
+            if (blockIdx.x == 0 && c == args.skip_load) continue;
             const uint32_t dst = sbase + kSlotOff + s * kTileBytes;
             const CUtensorMap* tm = kv == 0 ? &tm_k : &tm_v;
             mbar_arrive_expect_tx(bar(kSlotFull + s), kTileBytes);
+            issued = (issued & ~(1u << s)) | (1u << (s + 8)) |
+                     (static_cast<uint32_t>((c / kSlots) & 1) << s);
             QWA_TR(kTrK + kv, c >> 1);
             tma_load_3d(dst, tm, bar(kSlotFull + s), 0, g, krow);
             tma_load_3d(dst + kHalfBytes, tm, bar(kSlotFull + s), 64, g, krow);
           }
         }
       }
+      // Every issued copy has landed before the CTA exits (after an abort some
+      // were never consumed). At most one phase per slot or buffer is in
+      // flight, so the last issued parity identifies it.
+      bool drained = true;
+      for (int i = 0; i < kSlots + 2; ++i)
+        if ((issued >> (i + 8)) & 1u)
+          drained &= mbar_drain(i < kSlots ? bar(kSlotFull + i) : bar(kQFull + i - kSlots),
+                                (issued >> i) & 1u, *wait_limit);
+      if (!drained) atomicCAS(args.status, 0, kDevTimeoutDrain);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
@@ -211,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t qa = q_desc0 + ((qb * kQBufBytes) >> 4);
         const uint64_t qbd = qa + (kTileBytes >> 4);
         if (!(ok = mbar_wait(bar(kQFull + qb), (li >> 1) & 1, abort_flag, args.status,
-                             kDevTimeoutQ)))
+                             kDevTimeoutQ, wait_limit)))
           break;
         for (int j = 0; j < sch.n; ++j, ++t) {
           const int ck = 2 * t, sk = ck % kSlots;
@@ -219,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t k_desc = k_desc0 + ((sk * kTileBytes) >> 4);
           QWA_TR(kTrMmaKWait, t);
           if (!(ok = mbar_wait(bar(kSlotFull + sk), (ck / kSlots) & 1, abort_flag, args.status,
-                               kDevTimeoutSlotFull)))
+                               kDevTimeoutSlotFull, wait_limit)))
             break;
           tc_fence_after();
           QWA_TR(kTrMmaSA, t);
@@ -231,13 +258,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (have_prev) {
             const uint64_t vd = v_desc0 + ((prev_v * kTileBytes) >> 4);
             if (!(ok = mbar_wait(bar(kPLo + 1), (t - 1) & 1, abort_flag, args.status,
-                                 kDevTimeoutPFull)))
+                                 kDevTimeoutPFull, wait_limit)))
               break;
             tc_fence_after();
             QWA_TR(kTrMmaPVB, t - 1);
             issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 0);
             if (!(ok = mbar_wait(bar(kPHi + 1), (t - 1) & 1, abort_flag, args.status,
-                                 kDevTimeoutPFull)))
+                                 kDevTimeoutPFull, wait_limit)))
               break;
             tc_fence_after();
             QWA_TR(kTrMmaPHiB, t - 1);
@@ -250,18 +277,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(bar(kSFull + 1));
           tc_commit(bar(kSlotEmpty + sk));
           if (!(ok = mbar_wait(bar(kSlotFull + sv), (cv / kSlots) & 1, abort_flag, args.status,
-                               kDevTimeoutSlotFull)))
+                               kDevTimeoutSlotFull, wait_limit)))
             break;
           {
             const uint64_t vd = v_desc0 + ((sv * kTileBytes) >> 4);
             if (!(ok = mbar_wait(bar(kPLo + 0), t & 1, abort_flag, args.status,
-                                 kDevTimeoutPFull)))
+                                 kDevTimeoutPFull, wait_limit)))
               break;
             tc_fence_after();
             QWA_TR(kTrMmaPVA, t);
             issue_pv_half(t_o[0], t_s[0], vd, j > 0, width / 16, 0);
             if (!(ok = mbar_wait(bar(kPHi + 0), t & 1, abort_flag, args.status,
-                                 kDevTimeoutPFull)))
+                                 kDevTimeoutPFull, wait_limit)))
               break;
             tc_fence_after();
             QWA_TR(kTrMmaPHiA, t);
@@ -278,17 +305,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (ok && have_prev &&
-          mbar_wait(bar(kPLo + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
+          mbar_wait(bar(kPLo + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull, wait_limit)) {
         const uint64_t vd = v_desc0 + ((prev_v * kTileBytes) >> 4);
         tc_fence_after();
         issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 0);
-        if (mbar_wait(bar(kPHi + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull)) {
+        if (mbar_wait(bar(kPHi + 1), (t - 1) & 1, abort_flag, args.status, kDevTimeoutPFull, wait_limit)) {
           tc_fence_after();
           issue_pv_half(t_o[1], t_s[1], vd, prev_j > 0, prev_nk, 1);
           tc_commit(bar(kSlotEmpty + prev_v));
           tc_commit(bar(kOFinal + 1));
         }
       }
+      // Every issued MMA has completed before TMEM is released (after an abort
+      // nothing else waits for them).
+      tc_commit(bar(kDrain));
+      if (!mbar_drain(bar(kDrain), 0, *wait_limit)) atomicCAS(args.status, 0, kDevTimeoutDrain);
     }
   } else {
     // ------------------------------------------------------------- softmax
@@ -314,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_run = -INFINITY;  // running max of scaled scores (log2 domain)
       float l_run = 0.f;        // running denominator relative to m_run
       for (int j = 0; j < sch.n; ++j, ++t) {
-        if (!(ok = mbar_wait(bar(kSFull + x), t & 1, abort_flag, args.status, kDevTimeoutSFull)))
+        if (!(ok = mbar_wait(bar(kSFull + x), t & 1, abort_flag, args.status, kDevTimeoutSFull, wait_limit)))
           break;
         tc_fence_after();
         if (row == 0) QWA_TR(kTrSmSReady + x, t);
@@ -415,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Epilogue. O_X is read to registers (wait::ld) before this warpgroup's
       // next P arrival, which is what the next item's first PV_X waits for.
       if (!ok || !(ok = mbar_wait(bar(kOFinal + x), li & 1, abort_flag, args.status,
-                                  kDevTimeoutOFinal)))
+                                  kDevTimeoutOFinal, wait_limit)))
         break;
       tc_fence_after();
       if (row == 0) QWA_TR(kTrEpi + x, t - 1);
@@ -455,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(bar(kOStaged + x));
         if (row == 0) {
           ok = mbar_wait(bar(kOStaged + x), n_staged & 1, abort_flag, args.status,
-                         kDevTimeoutOStaged);
+                         kDevTimeoutOStaged, wait_limit);
           if (ok) {
             tma_store_3d(&tm_o, obuf, 0, 2 * g + x, row0);
             tma_store_3d(&tm_o, obuf + kHalfBytes, 64, 2 * g + x, row0);

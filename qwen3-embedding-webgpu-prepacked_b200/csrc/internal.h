@@ -1,5 +1,6 @@
 // Internal declarations shared by the .cu files of libqwa (not part of the ABI).
 #pragma once
+#include <cstddef>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -12,12 +13,32 @@ constexpr int kKVHeads = 8;
 constexpr int kHeadDim = 128;
 constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // keys per tile
+constexpr int kSparseMaxSeq = 8192;             // src/webgpu/ops.ts:328
+constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128), ops.ts:224
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Attention mode -> 1 (sparse keep rule) or 0 (full causal). AUTO follows
+// the reference: the sparse rule whenever the longest request has at most
+// 8192 tokens (ops.ts:328). Modes are the qwa_mode values 0/1/2.
+inline int resolve_sparse(int mode, int max_len) {
+  if (mode == 1) return 0;
+  if (mode == 2) return 1;
+  return max_len <= kSparseMaxSeq ? 1 : 0;
+}
 
 // One unit of attention work: a 128-row query tile of one request for the
 // two query heads (2g, 2g+1) that share key/value head g.
 //   x = global row of the tile's first query, y = its position in the request,
 //   z = request length, w = kv head g.
 using AttnItem = int4;
+
+// Work items of a packed batch: one per 128-row query tile per kv head.
+inline size_t count_work_items(const int32_t* cu, int batch) {
+  size_t n = 0;
+  for (int b = 0; b < batch; ++b)
+    n += static_cast<size_t>((cu[b + 1] - cu[b] + kBlockM - 1) / kBlockM) * kKVHeads;
+  return n;
+}
 
 // Key-tile schedule of one query tile. Shared by host (work counts, plan
 // ordering) and device (every warp role walks the same sequence).
@@ -77,6 +98,8 @@ struct AttnArgs {
   float scale_log2;  // softmax scale * log2(e)
   int* status;       // device status word (DeviceError codes)
   unsigned long long* trace;  // QWA_TRACE builds only: per-role clock64 timeline
+  unsigned long long wait_ns = 2000000000ull;  // bounded-wait limit of every mbarrier wait
+  int skip_load = -1;  // test hook: CTA 0 never issues its K/V load number skip_load
 };
 
 // Timeline layout of a QWA_TRACE build: trace[(cta * kTraceEvents + event) *

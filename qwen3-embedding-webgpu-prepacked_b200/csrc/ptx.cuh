@@ -22,6 +22,7 @@ enum DeviceError : int {
   kDevTimeoutPFull = 0x105,
   kDevTimeoutOFinal = 0x106,
   kDevTimeoutOStaged = 0x107,
+  kDevTimeoutDrain = 0x108,
   kDevTimeoutGemmEmpty = 0x201,
   kDevTimeoutGemmFull = 0x202,
   kDevTimeoutAccEmpty = 0x203,
@@ -67,21 +68,52 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Wait for the phase of `bar` with parity `parity` to complete. Returns false
 // (after recording `code` in *err and raising *abort) if it does not complete
-// within kWaitTimeoutNs, or if another role of the CTA has already aborted.
+// within limit_ns, or if another role of the CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          int* err, int code) {
+                                          int* err, int code,
+                                          uint64_t limit_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort = 1;
       atomicCAS(err, 0, code);
       return false;
     }
   }
+}
+
+// The same with the limit read from shared memory, only once a wait is slow
+// (a limit held in a register for the whole kernel costs the softmax warps
+// registers they need).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          int* err, int code,
+                                          const volatile unsigned long long* limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > *limit_ns) {
+      *abort = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+// Wait (at most limit_ns, no abort check) for a phase that is known to be in
+// flight: used after an abort to let issued copies and MMAs land before the
+// CTA releases the shared and tensor memory they write.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer() - t0 > limit_ns) return false;
+  return true;
 }
 
 // ----------------------------------------------------------------------- TMA
