@@ -211,6 +211,26 @@ QWA_API qwa_status qwa_rms_norm(qwa_ctx *ctx, void *x, const void *residual, con
                                 void *normalized, int rows, int width, float eps,
                                 int has_residual, void *stream);
 
+/* SwiGLU of the FFN. Replaces swigluShader / SwiGLUKernel.createRun(combined,
+ * output, rows, width) (src/webgpu/ops.ts:74-102): combined f16 [rows,
+ * 2*width] (the ffn_gate_up projection: gate columns, then up columns), out
+ * f16 [rows, width] = f16(g / (1 + exp(-g)) * u) in f32 arithmetic. width a
+ * positive multiple of 8; pointers 16-byte aligned. */
+QWA_API qwa_status qwa_swiglu(qwa_ctx *ctx, const void *combined, void *out, int rows, int width,
+                              void *stream);
+
+/* Token embedding lookup from a Q6_K matrix. Replaces embeddingShader /
+ * EmbeddingLookupKernel.createRun(tokens, weights, output, tokenCount, width)
+ * (src/webgpu/ops.ts:381-426): out f16 [tokens, width], row t = row
+ * ids[t] of the Q6_K matrix `table` [vocab, width] (210-byte blocks of 256
+ * values, src/gguf/quantization.ts:46-72), each value f16((d * scale) * q) in
+ * f32 like the shader. ids_device: DEVICE uint32 [tokens]; an id >= vocab
+ * gives a zero row (the reference does not check). width a positive
+ * multiple of 256; out 16-byte, table 2-byte, ids 4-byte aligned. */
+QWA_API qwa_status qwa_embedding_lookup_q6k(qwa_ctx *ctx, const uint32_t *ids_device,
+                                            const void *table, int vocab, void *out, int tokens,
+                                            int width, void *stream);
+
 /* Projection GEMM, f16: output[m, n] = sum_k input[m, k] * weight[n, k],
  * f32 accumulation on the tensor cores, f16 result. input f16 [m, k] and
  * weight f16 [n, k] row-major, output f16 [m, n] row-major. Replaces the

@@ -8,6 +8,6 @@ QKNormRopeKernel / CausalAttentionKernel interface (src/webgpu/ops.ts).
 The directory name is not a Python identifier; import it with
 ``importlib.import_module("qwen3-embedding-webgpu-prepacked_b200")``.
 """
-from . import _lib, attention, engine, executor, matmul, norm, pooling, prepacked, sharding, workloads  # noqa: F401
+from . import _lib, attention, engine, executor, ffn, matmul, model, norm, pooling, prepacked, sharding, workloads  # noqa: F401
 
-__all__ = ["_lib", "attention", "engine", "executor", "matmul", "norm", "pooling", "prepacked", "sharding", "workloads"]
+__all__ = ["_lib", "attention", "engine", "executor", "ffn", "matmul", "model", "norm", "pooling", "prepacked", "sharding", "workloads"]

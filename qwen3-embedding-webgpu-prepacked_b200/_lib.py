@@ -45,6 +45,8 @@ SIGNATURES = {
     "qwa_qkv_projection": (I32, [P, P, P, I32, P, P, P, P, P, I32P, I32, F32, F32, P, P]),
     "qwa_q40_qkv_projection": (I32, [P, P, P, I32, P, P, P, P, P, I32P, I32, F32, F32, P, P]),
     "qwa_rms_norm": (I32, [P, P, P, P, P, I32, I32, F32, I32, P]),
+    "qwa_swiglu": (I32, [P, P, P, I32, I32, P]),
+    "qwa_embedding_lookup_q6k": (I32, [P, P, P, I32, P, I32, I32, P]),
     "qwa_last_token_pool": (I32, [P, P, I32, P, I32P, I32, P]),
     "qwa_last_token_pool_padded": (I32, [P, P, P, P, I32, I32, I32, P]),
 }

@@ -699,6 +699,43 @@ qwa_status qwa_rms_norm(qwa_ctx* ctx, void* x, const void* residual, const float
   return QWA_OK;
 }
 
+qwa_status qwa_swiglu(qwa_ctx* ctx, const void* combined, void* out, int rows, int width,
+                      void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  if (rows < 0) return fail(ctx, QWA_ERR_INVALID_ARG, "rows must be >= 0");
+  if (width < 8 || width % 8 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "width must be a positive multiple of 8 (got %d)", width);
+  if (rows == 0) return QWA_OK;
+  if (!combined || !out) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(combined) || !aligned16(out))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  QWA_CUDA(ctx, launch_swiglu(static_cast<const __half*>(combined), static_cast<__half*>(out),
+                              rows, width, static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
+qwa_status qwa_embedding_lookup_q6k(qwa_ctx* ctx, const uint32_t* ids_device, const void* table,
+                                    int vocab, void* out, int tokens, int width, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  if (tokens < 0 || vocab < 0) return fail(ctx, QWA_ERR_INVALID_ARG, "tokens and vocab must be >= 0");
+  if (width < 256 || width % 256 != 0)
+    return fail(ctx, QWA_ERR_INVALID_ARG, "width must be a positive multiple of 256 (got %d)",
+                width);
+  if (tokens == 0) return QWA_OK;
+  if (!ids_device || !out || (vocab > 0 && !table))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(out) || (reinterpret_cast<uintptr_t>(table) & 1u) ||
+      (reinterpret_cast<uintptr_t>(ids_device) & 3u))
+    return fail(ctx, QWA_ERR_INVALID_ARG,
+                "out must be 16-byte, table 2-byte and ids 4-byte aligned");
+  QWA_CUDA(ctx, launch_q6k_embedding(ids_device, static_cast<const uint8_t*>(table), vocab,
+                                     static_cast<__half*>(out), tokens, width,
+                                     static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
 qwa_status qwa_last_token_pool(qwa_ctx* ctx, const void* hidden, int width, float* out,
                                const int32_t* cu_seqlens_host, int batch, void* stream) {
   if (!ctx) return QWA_ERR_INVALID_ARG;

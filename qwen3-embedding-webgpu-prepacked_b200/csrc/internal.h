@@ -179,4 +179,12 @@ cudaError_t launch_rms_norm(__half* x, const __half* residual, const float* weig
                             __half* normalized, int rows, int width, bool has_residual, float eps,
                             cudaStream_t stream);
 
+// SwiGLU: out[r, c] = f16(silu(g) * u), g = combined[r, c], u = combined[r, width + c].
+cudaError_t launch_swiglu(const __half* combined, __half* out, int rows, int width,
+                          cudaStream_t stream);
+
+// Token rows of a Q6_K matrix [vocab, width] as f16; ids >= vocab give zeros.
+cudaError_t launch_q6k_embedding(const uint32_t* ids, const uint8_t* table, int vocab,
+                                 __half* out, int tokens, int width, cudaStream_t stream);
+
 }  // namespace qwa

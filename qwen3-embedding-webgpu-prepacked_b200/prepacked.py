@@ -158,15 +158,35 @@ def parse_prepacked_model(buffer: bytes) -> PrepackedModel:
 
 
 def random_q40_rows(rng: np.random.Generator, n: int, k: int,
-                    scale: float = 0.02) -> np.ndarray:
+                    scale: float = 0.02, centered: bool = False) -> np.ndarray:
     """Seeded synthetic GGML Q4_0 bytes of an [n, k] matrix (k/32 blocks per
-    row): f16 scales |N(0, scale)|, nibbles uniform in [0, 16)."""
+    row): f16 scales |N(0, scale)|, nibbles uniform in [0, 16) -- or, with
+    ``centered``, in [1, 16), so the values scale * (q - 8) have mean zero
+    (a full model of such matrices keeps its residual stream unbiased)."""
     kb = k // 32
     out = np.empty((n, kb, Q40_BLOCK_BYTES), np.uint8)
     out[..., 0:2] = np.abs(rng.standard_normal((n, kb)) * scale).astype(np.float16) \
         .view(np.uint8).reshape(n, kb, 2)
-    out[..., 2:] = rng.integers(0, 256, size=(n, kb, 16), dtype=np.uint8)
+    if centered:
+        nib = rng.integers(1, 16, size=(n, kb, 32), dtype=np.uint8)
+        out[..., 2:] = nib[..., :16] | (nib[..., 16:] << 4)
+    else:
+        out[..., 2:] = rng.integers(0, 256, size=(n, kb, 16), dtype=np.uint8)
     return out.reshape(n, kb * Q40_BLOCK_BYTES)
+
+
+def random_q6k_rows(rng: np.random.Generator, vocab: int, width: int,
+                    d_scale: float = 0.002) -> np.ndarray:
+    """Seeded synthetic Q6_K bytes of a [vocab, width] matrix (210-byte blocks of
+    256 values, src/gguf/quantization.ts:46-72): random 6-bit quants, int8
+    scales in [-64, 64), d ~ |N(0, d_scale)| as f16."""
+    nb = width // 256
+    blk = rng.integers(0, 256, size=(vocab, nb, 210), dtype=np.uint8)
+    blk[:, :, 192:208] = rng.integers(-64, 64, size=(vocab, nb, 16)).astype(np.int8) \
+        .view(np.uint8)
+    blk[:, :, 208:210] = np.abs(rng.standard_normal((vocab, nb)) * d_scale) \
+        .astype(np.float16).view(np.uint8).reshape(vocab, nb, 2)
+    return blk.reshape(-1)
 
 
 def q40_part(name: str, rows: np.ndarray, k: int) -> Q40TensorPart:

@@ -1,0 +1,123 @@
+"""The whole embedding forward on the GPU: the Q6_K token-embedding lookup and
+SwiGLU kernels against the oracle, and the 28-layer model (model.py) against
+the chained CPU oracle (oracle/model.py), layer by layer.
+
+Tolerances: the lookup is bit-exact (the shader's f32 products, then f16);
+SwiGLU is within one f16 ulp of the exact value (the kernel's f32 result is
+rounded once). The chained model compares the residual stream after every
+layer and the final embeddings: each step's f32 accumulation differs from the
+exact sum, a stored f16 value can round the other way, and such one-ulp
+differences travel through 28 layers; the test prints their growth and
+requires per-layer cosine >= 0.9999 and embedding cosine >= 0.9999 (the
+reference's own batch-vs-single gate is 0.999, src/main.ts:314-316)."""
+import asyncio
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ffn as offn
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("width", [1024, 768])
+def test_q6k_embedding_lookup_bit_exact(pkg, cuda_dev, width):
+    rng = np.random.default_rng(width)
+    vocab = 300
+    table = pkg.prepacked.random_q6k_rows(rng, vocab, width)
+    ids = np.concatenate([rng.integers(0, vocab, 500), [0, vocab - 1, vocab, 2 ** 31]])
+    got = pkg.ffn.embedding_lookup(torch.from_numpy(ids.astype(np.int32)).cuda(),
+                                   torch.from_numpy(table).cuda(), width, vocab)
+    torch.cuda.synchronize()
+    ref = offn.embedding_lookup_f16(ids.astype(np.int64), table, vocab, width)
+    assert np.array_equal(got.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+    # against the exact values too: within half an f16 spacing plus f32 rounding
+    exact = offn.dequant_q6k(table, vocab, width)[ids[:500]]
+    assert np.all(np.abs(ref[:500].astype(np.float64) - exact)
+                  <= np.spacing(np.abs(ref[:500])).astype(np.float64))
+
+
+def test_q6k_reference_known_answer_on_device(pkg, cuda_dev):
+    block = np.zeros(210, np.uint8)  # tests/quantization.test.ts:35-42
+    block[192:208] = 1
+    block[208:210] = np.array([0x3c00], "<u2").view(np.uint8)
+    got = pkg.ffn.embedding_lookup(torch.zeros(2, dtype=torch.int32, device="cuda"),
+                                   torch.from_numpy(block).cuda(), 256, 1)
+    assert (got.cpu().float() == -32).all()
+
+
+@pytest.mark.parametrize("rows,width", [(1000, 3072), (3, 8), (0, 16)])
+def test_swiglu_within_one_ulp(pkg, cuda_dev, rows, width):
+    rng = np.random.default_rng(rows)
+    comb = (3 * rng.standard_normal((rows, 2 * width))).astype(np.float16)
+    got = pkg.ffn.swiglu(torch.from_numpy(comb).cuda(), width)
+    torch.cuda.synchronize()
+    ref = offn.swiglu(comb, width)
+    g = got.cpu().numpy().astype(np.float64)
+    assert np.all(np.abs(g - ref) <= np.spacing(np.abs(ref).astype(np.float16)).astype(np.float64))
+    if rows:
+        assert np.mean(g == ref.astype(np.float16).astype(np.float64)) > 0.99
+
+
+@pytest.fixture(scope="module")
+def synthetic_model(pkg):
+    data = pkg.model.synthetic_model_file(28, 4096, seed=0)
+    parsed = pkg.prepacked.parse_prepacked_model(data)
+    weights = pkg.prepacked.PrepackedWeights(parsed, 0)
+    return parsed, pkg.model.Qwen3EmbeddingModel(weights)
+
+
+def _cos_rows(a, b):
+    a, b = np.asarray(a, np.float64).reshape(len(a), -1), np.asarray(b, np.float64).reshape(
+        len(b), -1)
+    return (a * b).sum(1) / np.linalg.norm(a, axis=1) / np.linalg.norm(b, axis=1)
+
+
+def test_full_model_chain_against_oracle(pkg, cuda_dev, synthetic_model):
+    from oracle import model as omodel
+    parsed, model = synthetic_model
+    lengths = [50, 17, 130]
+    cu = [0] + [int(x) for x in np.cumsum(lengths)]
+    ids = np.random.default_rng(1).integers(0, 4096, cu[-1])
+    trace = []
+    emb = model.embed(torch.from_numpy(ids.astype(np.int32)).cuda(), cu)
+    model.forward(torch.from_numpy(ids.astype(np.int32)).cuda(), cu, trace=trace)
+    torch.cuda.synchronize()
+    ref_trace = []
+    ref = omodel.embed(parsed, ids, cu, 28, ref_trace)
+    growth = []
+    for l, (g, r) in enumerate(zip(trace, ref_trace)):
+        g = g.cpu().numpy().astype(np.float64)
+        r = r.astype(np.float64)
+        growth.append((l, float(np.abs(g - r).max()), float(_cos_rows(g, r).min())))
+    print("MODEL_CHAIN layer max-abs / min row cosine of the residual stream:", growth)
+    e = emb.cpu().numpy().astype(np.float64)
+    cos = (e * ref).sum(1)
+    print("MODEL_CHAIN embedding cosine per request:", cos.tolist(),
+          "max-abs", float(np.abs(e - ref).max()))
+    assert min(c for _, _, c in growth) >= 0.9999
+    assert cos.min() >= 0.9999
+
+
+def test_full_model_batch_equals_single_and_padded(pkg, cuda_dev, synthetic_model):
+    """The reference's batch-vs-single gate (src/main.ts:314-316, cosine >=
+    0.999) through the engine, for packed and padded micro-batches; packed
+    batches give each request exactly its single-request embedding."""
+    eng_mod = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.engine")
+    _, model = synthetic_model
+    rng = np.random.default_rng(5)
+    reqs = [list(rng.integers(0, 4095, size=n - 1)) + [4095] for n in (15, 700, 1, 150, 64)]
+
+    async def embed_all(packing, batch_size):
+        eng = eng_mod.EmbeddingEngine(model, None, batch_size, 0, 4095, packing=packing)
+        return await asyncio.gather(*[eng.submit_tokens(r) for r in reqs])
+
+    var = np.stack(asyncio.run(embed_all("varlen", 16)))
+    single = np.stack(asyncio.run(embed_all("varlen", 1)))
+    pad = np.stack(asyncio.run(embed_all("padded", 16)))
+    assert np.isfinite(var).all()
+    assert np.allclose(np.linalg.norm(var, axis=1), 1.0, atol=1e-5)
+    assert np.array_equal(var, single)
+    assert np.sum(var * pad, axis=1).min() >= 0.999
