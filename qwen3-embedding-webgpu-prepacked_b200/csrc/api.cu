@@ -34,8 +34,10 @@ constexpr size_t kMaxPlans = 64;
 
 struct Plan {
   int32_t* d_cu = nullptr;
-  AttnItem* d_items = nullptr;
+  AttnItem* d_items = nullptr;   // grouped by CTA, then the CTAs' first items (int)
+  const int* d_offsets = nullptr;  // inside d_items: CTA c runs items [off[c], off[c+1])
   int n_items = 0;
+  int n_ctas = 0;
   int batch = 0;
   int total = 0;
   int max_len = 0;
@@ -51,6 +53,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 struct qwa_ctx {
   int device = 0;
+  int sms = 148;  // persistent attention grid size
   std::string error;
   int* d_status = nullptr;
   float* d_rope = nullptr;
@@ -181,6 +184,80 @@ qwa_status check_cu(qwa_ctx* ctx, const int32_t* cu, int batch, int* total, int*
   return QWA_OK;
 }
 
+// Work schedule of an attention call. Items are one 128-row query tile x one
+// kv head; each gets a cost in key-tile periods (narrow tiles cost less, every
+// item pays a fixed fill/drain share). The items are dealt to `sms` CTAs by
+// list scheduling (each to the least-loaded CTA) in this order:
+// * longest first, which bounds the final imbalance (LPT);
+// * for full-causal calls on long requests, request batches first: the items
+//   of a few requests whose K/V fit well inside L2 are dealt before the next
+//   batch's, so the CTAs running at one time read the same K/V (longest first
+//   within a batch). Without it every wave touches every request's K/V and
+//   the K/V of earlier keys is re-read from HBM once per query tile.
+// Returns the items grouped by CTA and offsets[c]..offsets[c+1] per CTA.
+constexpr double kItemOverhead = 0.6;                   // periods per item
+constexpr int kGroupMinLen = 2048;                      // full causal, longest request
+constexpr int64_t kGroupKvBytes = 48ll << 20;           // K/V bytes per request batch
+std::vector<AttnItem> schedule_work(const int32_t* cu, int batch, int sparse, int prefix,
+                                    int window, int sms, std::vector<int>* offsets) {
+  struct Work {
+    double cost;
+    int group;
+    AttnItem item;
+  };
+  int max_len = 0;
+  for (int b = 0; b < batch; ++b) max_len = std::max(max_len, cu[b + 1] - cu[b]);
+  const bool grouped = !sparse && max_len >= kGroupMinLen;
+  std::vector<Work> work;
+  int group = 0;
+  int64_t group_bytes = 0;
+  for (int b = 0; b < batch; ++b) {
+    const int len = cu[b + 1] - cu[b];
+    const int64_t kv_bytes = static_cast<int64_t>(len) * kKVHeads * kHeadDim * 2 * 2;
+    if (grouped && group_bytes > 0 && group_bytes + kv_bytes > kGroupKvBytes) {
+      ++group;
+      group_bytes = 0;
+    }
+    group_bytes += kv_bytes;
+    for (int q0 = 0; q0 < len; q0 += kBlockM) {
+      const KeySchedule s = make_key_schedule(q0, len, sparse, prefix, window);
+      const int q_last = std::min(q0 + kBlockM, len) - 1;
+      double cost = kItemOverhead;
+      for (int j = 0; j < s.n; ++j)
+        cost += 0.35 + 0.65 * key_tile_width(s, j, q_last, prefix) / double(kBlockN);
+      for (int g = 0; g < kKVHeads; ++g)
+        work.push_back({cost, grouped ? group : 0, make_int4(cu[b] + q0, q0, len, g)});
+    }
+  }
+  std::stable_sort(work.begin(), work.end(), [](const Work& a, const Work& b) {
+    return a.group != b.group ? a.group < b.group : a.cost > b.cost;
+  });
+  const int n_ctas = static_cast<int>(std::min<size_t>(work.size(), static_cast<size_t>(sms)));
+  std::vector<std::vector<int>> per_cta(n_ctas);
+  // min-heap of (load, cta)
+  std::vector<std::pair<double, int>> heap;
+  for (int c = 0; c < n_ctas; ++c) heap.push_back({0.0, c});
+  auto cmp = [](const std::pair<double, int>& a, const std::pair<double, int>& b) {
+    return a.first != b.first ? a.first > b.first : a.second > b.second;
+  };
+  std::make_heap(heap.begin(), heap.end(), cmp);
+  for (size_t i = 0; i < work.size(); ++i) {
+    std::pop_heap(heap.begin(), heap.end(), cmp);
+    auto& top = heap.back();
+    per_cta[top.second].push_back(static_cast<int>(i));
+    top.first += work[i].cost;
+    std::push_heap(heap.begin(), heap.end(), cmp);
+  }
+  std::vector<AttnItem> items;
+  items.reserve(work.size());
+  offsets->assign(1, 0);
+  for (int c = 0; c < n_ctas; ++c) {
+    for (int i : per_cta[c]) items.push_back(work[i].item);
+    offsets->push_back(static_cast<int>(items.size()));
+  }
+  return items;
+}
+
 // Plan lookup/creation. sparse < 0 requests a plan without attention items
 // (the prologue only needs the device cu_seqlens).
 qwa_status get_plan(qwa_ctx* ctx, const int32_t* cu, int batch, int sparse, int prefix,
@@ -204,29 +281,23 @@ qwa_status get_plan(qwa_ctx* ctx, const int32_t* cu, int batch, int sparse, int 
   QWA_CUDA(ctx, cudaMemcpyAsync(plan->d_cu, cu, sizeof(int32_t) * (batch + 1),
                                 cudaMemcpyHostToDevice, stream));
   if (sparse >= 0) {
-    struct Work {
-      int tiles;
-      AttnItem item;
-    };
-    std::vector<Work> work;
-    for (int b = 0; b < batch; ++b) {
-      const int len = cu[b + 1] - cu[b];
-      for (int q0 = 0; q0 < len; q0 += kBlockM) {
-        const KeySchedule s = make_key_schedule(q0, len, sparse, prefix, window);
-        for (int g = 0; g < kKVHeads; ++g) work.push_back({s.n, make_int4(cu[b] + q0, q0, len, g)});
-      }
-    }
-    // Longest-first: the block scheduler dispatches in blockIdx order, which
-    // approximates LPT over the causal triangle.
-    std::stable_sort(work.begin(), work.end(),
-                     [](const Work& a, const Work& b) { return a.tiles > b.tiles; });
-    std::vector<AttnItem> items(work.size());
-    for (size_t i = 0; i < work.size(); ++i) items[i] = work[i].item;
+    std::vector<int> offsets;
+    std::vector<AttnItem> items = schedule_work(cu, batch, sparse, prefix, window, ctx->sms,
+                                                &offsets);
     plan->n_items = static_cast<int>(items.size());
+    plan->n_ctas = static_cast<int>(offsets.size()) - 1;
     if (!items.empty()) {
-      QWA_CUDA(ctx, cudaMalloc(&plan->d_items, sizeof(AttnItem) * items.size()));
-      QWA_CUDA(ctx, cudaMemcpyAsync(plan->d_items, items.data(), sizeof(AttnItem) * items.size(),
-                                    cudaMemcpyHostToDevice, stream));
+      const size_t item_bytes = sizeof(AttnItem) * items.size();
+      const size_t bytes = item_bytes + sizeof(int) * offsets.size();
+      std::vector<uint8_t> host(bytes);
+      std::memcpy(host.data(), items.data(), item_bytes);
+      std::memcpy(host.data() + item_bytes, offsets.data(), sizeof(int) * offsets.size());
+      QWA_CUDA(ctx, cudaMalloc(&plan->d_items, bytes));
+      QWA_CUDA(ctx, cudaMemcpyAsync(plan->d_items, host.data(), bytes, cudaMemcpyHostToDevice,
+                                    stream));
+      // pageable source: the copy is staged before cudaMemcpyAsync returns
+      plan->d_offsets = reinterpret_cast<const int*>(
+          reinterpret_cast<const uint8_t*>(plan->d_items) + item_bytes);
     }
   }
   if (ctx->plans.size() >= kMaxPlans) {
@@ -349,6 +420,8 @@ qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void*
   args.trace = ctx->trace;
   args.wait_ns = ctx->wait_ns;
   args.skip_load = ctx->skip_load;
+  args.cta_offsets = plan->d_offsets;
+  args.num_ctas = plan->n_ctas;
   QWA_CUDA(ctx, launch_attention(tm_q, tm_k, tm_v, tm_o, args, plan->n_items, stream));
   return QWA_OK;
 }
@@ -388,6 +461,7 @@ qwa_status qwa_create(int device, qwa_ctx** out) {
   DeviceGuard guard(device);
   auto ctx = std::make_unique<qwa_ctx>();
   ctx->device = device;
+  ctx->sms = prop.multiProcessorCount;
   if (cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess) return QWA_ERR_CUDA;
   if (cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess) return QWA_ERR_CUDA;
   if (ensure_encode(ctx.get()) != QWA_OK) return QWA_ERR_CUDA;

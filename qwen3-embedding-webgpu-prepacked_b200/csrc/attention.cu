@@ -142,10 +142,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  // Work items of this CTA: blockIdx.x, blockIdx.x + gridDim.x, ... (the
-  // list is sorted longest first). li counts this CTA's items, t its key
-  // tiles across items; every role walks the same sequence, so barrier
-  // phases follow from li and t.
+  // Work items of this CTA: its own list from the plan's schedule (longest
+  // first), or blockIdx.x, blockIdx.x + gridDim.x, ... without one. li counts
+  // this CTA's items, t its key tiles across items; every role walks the same
+  // sequence, so barrier phases follow from li and t.
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
@@ -155,12 +155,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 3-4): bit i+8 set once one was issued, bit i its parity. Waited for
       // before exit so no copy lands after it.
       uint32_t issued = 0;
-      AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
-      for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
+      const ItemRange rng = item_range(args, num_items);
+      AttnItem next_item = rng.beg < rng.end ? args.items[rng.beg] : AttnItem{};
+      for (int it = rng.beg, li = 0; ok && it < rng.end; it += rng.stride, ++li) {
         // the next item's descriptor is loaded one item ahead (a global load
         // at every item boundary sat on each role's critical path)
         const AttnItem item = next_item;
-        if (it + static_cast<int>(gridDim.x) < num_items) next_item = args.items[it + gridDim.x];
+        if (it + rng.stride < rng.end) next_item = args.items[it + rng.stride];
         const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
         const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
         const int qb = li & 1;
@@ -226,12 +227,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool have_prev = false;  // PV_B of the previous tile still to issue
       int prev_v = 0, prev_j = 0, prev_nk = 8;
       bool prev_last = false;
-      AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
-      for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
+      const ItemRange rng = item_range(args, num_items);
+      AttnItem next_item = rng.beg < rng.end ? args.items[rng.beg] : AttnItem{};
+      for (int it = rng.beg, li = 0; ok && it < rng.end; it += rng.stride, ++li) {
         // the next item's descriptor is loaded one item ahead (a global load
         // at every item boundary sat on each role's critical path)
         const AttnItem item = next_item;
-        if (it + static_cast<int>(gridDim.x) < num_items) next_item = args.items[it + gridDim.x];
+        if (it + rng.stride < rng.end) next_item = args.items[it + rng.stride];
         const KeySchedule sch = make_key_schedule(item.y, item.z, sparse, prefix, window);
         const int q_last = (item.y + kBlockM < item.z ? item.y + kBlockM : item.z) - 1;
         const int qb = li & 1;
@@ -334,10 +336,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int t = 0;
     int n_staged = 0;  // full query tiles this head has staged (kOStaged phase)
     int q_release = -1;  // row 0: Q buffer to release once its O stores read it
-    AttnItem next_item = blockIdx.x < num_items ? args.items[blockIdx.x] : AttnItem{};
-    for (int it = blockIdx.x, li = 0; ok && it < num_items; it += gridDim.x, ++li) {
+    const ItemRange rng = item_range(args, num_items);
+    AttnItem next_item = rng.beg < rng.end ? args.items[rng.beg] : AttnItem{};
+    for (int it = rng.beg, li = 0; ok && it < rng.end; it += rng.stride, ++li) {
       const AttnItem item = next_item;
-      if (it + static_cast<int>(gridDim.x) < num_items) next_item = args.items[it + gridDim.x];
+      if (it + rng.stride < rng.end) next_item = args.items[it + rng.stride];
       const int row0 = item.x, q0 = item.y, len = item.z, g = item.w;
       const KeySchedule sch = make_key_schedule(q0, len, sparse, prefix, window);
       const int q = q0 + row;
@@ -659,7 +662,9 @@ cudaError_t launch_attention(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
   }
   if (num_items <= 0) return cudaSuccess;
   const int sm_count = sms[dev];
-  const int grid = num_items < sm_count ? num_items : sm_count;  // persistent: one CTA per SM
+  // persistent: one CTA per SM, or the plan's per-CTA item lists
+  const int grid = args.cta_offsets ? args.num_ctas
+                                    : (num_items < sm_count ? num_items : sm_count);
   attention_kernel<<<grid, kThreads, kSmemBytes, stream>>>(tm_q, tm_k, tm_v, tm_o, args,
                                                            num_items);
   return cudaGetLastError();

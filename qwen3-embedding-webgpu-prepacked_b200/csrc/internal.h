@@ -100,7 +100,21 @@ struct AttnArgs {
   unsigned long long* trace;  // QWA_TRACE builds only: per-role clock64 timeline
   unsigned long long wait_ns = 2000000000ull;  // bounded-wait limit of every mbarrier wait
   int skip_load = -1;  // test hook: CTA 0 never issues its K/V load number skip_load
+  // Per-CTA item lists: CTA c runs items [cta_offsets[c], cta_offsets[c+1]) of
+  // a grid of num_ctas. nullptr: CTA c runs items c, c + grid, c + 2 grid, ...
+  const int* cta_offsets = nullptr;
+  int num_ctas = 0;
 };
+
+// The items one CTA runs: it = beg, beg + stride, ... < end.
+struct ItemRange {
+  int beg, end, stride;
+};
+__device__ __forceinline__ ItemRange item_range(const AttnArgs& a, int num_items) {
+  if (a.cta_offsets)
+    return {a.cta_offsets[blockIdx.x], a.cta_offsets[blockIdx.x + 1], 1};
+  return {static_cast<int>(blockIdx.x), num_items, static_cast<int>(gridDim.x)};
+}
 
 // Timeline layout of a QWA_TRACE build: trace[(cta * kTraceEvents + event) *
 // kTraceIters + key_tile] = clock64() for the first kTraceCtas CTAs (key_tile
