@@ -6,6 +6,7 @@ tensor-map encoder at run time, so it loads on a machine without a GPU
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import subprocess
 import sys
@@ -28,13 +29,27 @@ def nvcc() -> str:
     return cand if os.path.exists(cand) else "nvcc"
 
 
+STAMP = LIB + ".stamp"  # content hash of what built LIB (kept out of git like the .so)
+
+
+def _fingerprint() -> str:
+    """sha256 over every source, header, this file and the flags: a copy of the
+    tree (with file times reset) rebuilds exactly when its contents differ."""
+    h = hashlib.sha256()
+    for d in SOURCES + HEADERS:
+        with open(os.path.join(CSRC, d), "rb") as f:
+            h.update(d.encode() + b"\0" + f.read())
+    with open(os.path.abspath(__file__), "rb") as f:
+        h.update(f.read())
+    h.update(" ".join(NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
 def _stale() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(STAMP):
         return True
-    t = os.path.getmtime(LIB)
-    deps = SOURCES + HEADERS + [os.path.basename(__file__)]
-    return any(os.path.getmtime(os.path.join(CSRC if not d.endswith(".py") else HERE, d)) > t
-               for d in deps)
+    with open(STAMP) as f:
+        return f.read().strip() != _fingerprint()
 
 
 TRACE_LIB = os.path.join(HERE, "libqwa_trace.so")
@@ -61,6 +76,9 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> st
     os.replace(tmp, lib)
     for o in objs:
         os.remove(o)
+    if not trace:
+        with open(STAMP, "w") as f:
+            f.write(_fingerprint() + "\n")
     return lib
 
 

@@ -48,7 +48,9 @@ enum TraceEvent : int {
   kTrSmSReady, kTrSmLoaded = kTrSmSReady + 2, kTrSmMax = kTrSmLoaded + 2,
   kTrSmExp = kTrSmMax + 2, kTrSmArrive = kTrSmExp + 2, kTrEpi = kTrSmArrive + 2,
   kTrEpiEnd = kTrEpi + 2, kTrMmaPHiA = kTrEpiEnd + 2, kTrMmaKWait, kTrMmaPHiB,
-  kTrMmaPVAHiDone, kTrMmaSADone
+  kTrMmaPVAHiDone, kTrMmaSADone,
+  kTrWarpMax,             // +softmax warp (0..7): lane 0 after the row max
+  kTrWarpArrive = kTrWarpMax + 8  // +softmax warp: lane 0 at its P-hi arrival
 };
 #define QWA_TR(ev, j)                                                                \
   do {                                                                               \
@@ -398,6 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_run = m_new;
         }
         if (row == 0) QWA_TR(kTrSmMax + x, t);
+        if (lane == 0) QWA_TR(kTrWarpMax + warp - 2, t);
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
         // P is published in two halves so PV's first four K steps (keys
         // 0..63) run on the tensor pipe while keys 64..127 are exponentiated.
@@ -440,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row == 0) QWA_TR(kTrSmExp + x, t);
         mbar_arrive(bar(kPHi + x));
         if (row == 0) QWA_TR(kTrSmArrive + x, t);
+        if (lane == 0) QWA_TR(kTrWarpArrive + warp - 2, t);
         if (q_release >= 0) {  // row 0 only: see the epilogue
           bulk_wait_read();
           mbar_arrive(bar(kQEmpty + q_release));
