@@ -50,7 +50,12 @@ enum TraceEvent : int {
   kTrEpiEnd = kTrEpi + 2, kTrMmaPHiA = kTrEpiEnd + 2, kTrMmaKWait, kTrMmaPHiB,
   kTrMmaPVAHiDone, kTrMmaSADone,
   kTrWarpMax,             // +softmax warp (0..7): lane 0 after the row max
-  kTrWarpArrive = kTrWarpMax + 8  // +softmax warp: lane 0 at its P-hi arrival
+  kTrWarpArrive = kTrWarpMax + 8,   // +softmax warp: lane 0 at its P-hi arrival
+  kTrEpiChunk = kTrWarpArrive + 8,  // +X*4+c: row 0 after O chunk c is staged
+  kTrEpiStaged = kTrEpiChunk + 8,   // +X: row 0 once all four warps staged
+  kTrEpiIssued = kTrEpiStaged + 2,  // +X: row 0 after the stores are issued
+  kTrWarpEpi = kTrEpiIssued + 2,    // +softmax warp: lane 0 past the O-final wait
+  kTrWarpStaged = kTrWarpEpi + 8    // +softmax warp: lane 0 at its staged arrival
 };
 #define QWA_TR(ev, j)                                                                \
   do {                                                                               \
@@ -457,6 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       tc_fence_after();
       if (row == 0) QWA_TR(kTrEpi + x, t - 1);
+      if (lane == 0) QWA_TR(kTrWarpEpi + warp - 2, t - 1);
       const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
       const int qb = li & 1;
       if (q0 + kBlockM <= len) {
@@ -484,6 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          "r"(w0), "r"(w1), "r"(w2), "r"(w3)
                          : "memory");
           }
+          if (row == 0) QWA_TR(kTrEpiChunk + x * 4 + c, t - 1);
         }
         // Each warp publishes its rows (proxy fence, then one arrival); only
         // the storing thread waits, with a bounded wait, so no warp can be
@@ -491,13 +498,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(kOStaged + x));
+        if (lane == 0) QWA_TR(kTrWarpStaged + warp - 2, t - 1);
         if (row == 0) {
           ok = mbar_wait(bar(kOStaged + x), n_staged & 1, abort_flag, args.status,
                          kDevTimeoutOStaged, wait_limit);
+          QWA_TR(kTrEpiStaged + x, t - 1);
           if (ok) {
             tma_store_3d(&tm_o, obuf, 0, 2 * g + x, row0);
             tma_store_3d(&tm_o, obuf + kHalfBytes, 64, 2 * g + x, row0);
             bulk_commit();
+            QWA_TR(kTrEpiIssued + x, t - 1);
             // The buffer may take a new Q only once the stores have read it.
             // That Q is needed one item later, so the wait and the release
             // happen after this head's next P arrival, off the epilogue.

@@ -120,7 +120,7 @@ __device__ __forceinline__ ItemRange item_range(const AttnArgs& a, int num_items
 // kTraceIters + key_tile] = clock64() for the first kTraceCtas CTAs (key_tile
 // counts the CTA's tiles across its work items).
 constexpr int kTraceCtas = 4;
-constexpr int kTraceEvents = 41;
+constexpr int kTraceEvents = 69;
 constexpr int kTraceIters = 256;
 
 // tm_o: the output [T, 16, 128] with tm_q's geometry (full query tiles are
