@@ -61,6 +61,9 @@ def parse():
                          "for profiling")
     ap.add_argument("--engine", action="store_true",
                     help="time the micro-batch engine, padded vs varlen packing (one GPU)")
+    ap.add_argument("--model", action="store_true",
+                    help="time the whole 28-layer embedding model (FFN included) through the "
+                         "engine, padded vs varlen packing (one GPU)")
     # profiling aids: shrink the workload (never used for the reported line)
     ap.add_argument("--requests", type=int, default=0, help="override request count")
     ap.add_argument("--layers", type=int, default=0, help="override layer count")
@@ -244,11 +247,13 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def run_engine(args):
+def run_engine(args, full_model=False):
     """Micro-batch engine: 16 requests of 15..5000 tokens through the 28-layer
-    attention stack, packed (varlen) vs padded to the longest request as the
-    reference does. Each step is one whole micro-batch through the engine's
-    public call (ids host->device, embeddings device->host included)."""
+    attention stack (or, with full_model, the whole embedding model: token
+    lookup, attention and FFN halves, output norm, pool), packed (varlen) vs
+    padded to the longest request as the reference does. Each step is one
+    whole micro-batch through the engine's public call (ids host->device,
+    embeddings device->host included)."""
     import asyncio
     import torch
     pkg = importlib.import_module(PKG)
@@ -257,7 +262,14 @@ def run_engine(args):
     torch.cuda.set_device(0)
     L = args.layers or pkg.workloads.LAYERS
     lengths = pkg.workloads.ragged_lengths(args.requests or 16, 15, 5000, 2025)
-    rt = eng_mod.AttentionStackRuntime(layers=L, seed=7)
+    if full_model:
+        # seeded weights of the model's shapes (no checkpoint), full vocabulary
+        data = pkg.model.synthetic_model_file(L, eng_mod.EOS_TOKEN + 1, seed=7)
+        weights = pkg.prepacked.PrepackedWeights(pkg.prepacked.parse_prepacked_model(data), 0)
+        rt = pkg.model.Qwen3EmbeddingModel(weights)
+        del data
+    else:
+        rt = eng_mod.AttentionStackRuntime(layers=L, seed=7)
     rng = np.random.default_rng(3)
     reqs = [list(rng.integers(0, eng_mod.EOS_TOKEN, size=n - 1)) + [eng_mod.EOS_TOKEN]
             for n in lengths]
@@ -335,15 +347,21 @@ def run_engine(args):
     peaks, psrc = measured_peaks()
     v = results["varlen"]
     line = {
-        "metric": "embedding micro-batch requests/s (engine, attention stack)",
+        "metric": ("embedding micro-batch requests/s (engine, whole model)" if full_model
+                   else "embedding micro-batch requests/s (engine, attention stack)"),
         "value": v["requests_per_s"], "unit": "requests/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": v["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic token ids; seeded random Q4_0 tile32 weights",
         "config": {"workload": "engine_mixed16", "lengths": list(lengths), "layers": L,
-                   "per_layer": "Q4_0 QKV projection with fused Q/K norm + RoPE (tcgen05), "
-                                "attention, Q4_0 O projection, residual + RMSNorm; then "
-                                "last-token pool",
+                   "per_layer": ("Q4_0 QKV projection with fused Q/K norm + RoPE (tcgen05), "
+                                 "attention, Q4_0 O projection, residual + RMSNorm, Q4_0 "
+                                 "gate_up projection, SwiGLU, Q4_0 down projection, residual + "
+                                 "RMSNorm; Q6_K token lookup before, last-token pool after"
+                                 if full_model else
+                                 "Q4_0 QKV projection with fused Q/K norm + RoPE (tcgen05), "
+                                 "attention, Q4_0 O projection, residual + RMSNorm; then "
+                                 "last-token pool"),
                    "packing": "varlen"},
         "packing": results,
         "varlen_speedup_over_padded": results["padded"]["ms_per_step"] / v["ms_per_step"],
@@ -444,8 +462,8 @@ def main():
     if args.gemm:
         run_gemm(args)
         return
-    if args.engine:
-        run_engine(args)
+    if args.engine or args.model:
+        run_engine(args, full_model=args.model)
         return
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
