@@ -66,3 +66,26 @@ def test_device_backend_rejects_nothing_for_an_idle_rank(pkg, cuda_dev):
         be.check()
     finally:
         be.close()
+
+
+def test_multi_device_executor_on_two_gpus(pkg, oracle, cuda_dev):
+    """The same split over two real devices (skipped on a one-GPU box)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ex = pkg.executor
+    lengths = [700, 17, 1300, 64, 5]
+    cu = [0] + list(np.cumsum(lengths))
+    T = cu[-1]
+    layers = _layers(T, 2, seed=3)
+    host_in = [torch.from_numpy(x).pin_memory() for x, _, _ in layers]
+    host_out = [torch.zeros(T, 16, 128, dtype=torch.float16).pin_memory() for _ in range(2)]
+    m = ex.MultiDeviceExecutor(lengths, [0, 1])
+    try:
+        m.set_weights([(qw, kw) for _, qw, kw in layers])
+        m.run(host_in, host_out)
+    finally:
+        m.close()
+    for l, (x, qw, kw) in enumerate(layers):
+        q, k = oracle.c_qk_norm_rope(x, qw, kw, cu)
+        ref = oracle.c_attention(q.astype(np.float16), k.astype(np.float16), x, 4096, 3072, cu)
+        assert np.abs(host_out[l].numpy().astype(np.float64) - ref).max() <= 2e-3
