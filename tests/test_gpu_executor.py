@@ -89,3 +89,38 @@ def test_multi_device_executor_on_two_gpus(pkg, oracle, cuda_dev):
         q, k = oracle.c_qk_norm_rope(x, qw, kw, cu)
         ref = oracle.c_attention(q.astype(np.float16), k.astype(np.float16), x, 4096, 3072, cu)
         assert np.abs(host_out[l].numpy().astype(np.float64) - ref).max() <= 2e-3
+
+
+def test_auto_mode_is_resolved_on_the_whole_batch(pkg, oracle, cuda_dev):
+    """A 9000-token request makes the reference's AUTO rule pick full causal for
+    the whole batch (ops.ts:328). The shard that holds only the 1000-token
+    request must run full causal too (on its own it would pick the sparse
+    rule, which drops keys of rows past 608)."""
+    ex = pkg.executor
+    lengths = [9000, 1000]
+    plan = ex.ShardPlan(lengths, 2)
+    assert plan.resolved_mode == ex.MODE_FULL
+    assert sorted(len(r) for r in plan.assignment) == [1, 1]
+    cu = [0, 9000, 10000]
+    layers = _layers(10000, 1, seed=9)
+    host_in = [torch.from_numpy(layers[0][0]).pin_memory()]
+    host_out = [torch.zeros(10000, 16, 128, dtype=torch.float16).pin_memory()]
+    m = ex.MultiDeviceExecutor(lengths, [0, 0])
+    try:
+        m.set_weights([(layers[0][1], layers[0][2])])
+        m.run(host_in, host_out)
+    finally:
+        m.close()
+    x, qw, kw = layers[0]
+    one = pkg.attention.prefill_attention_layer(torch.from_numpy(x).to(cuda_dev),
+                                                torch.from_numpy(qw).to(cuda_dev),
+                                                torch.from_numpy(kw).to(cuda_dev), cu)
+    torch.cuda.synchronize()
+    assert torch.equal(one.cpu(), host_out[0])
+    # rows of the short request past 608 against the full-causal oracle
+    q, k = oracle.c_qk_norm_rope(x, qw, kw, cu)
+    rows = np.array([(9000 + t) * 16 + h for t in (0, 607, 608, 700, 999) for h in (0, 5, 15)])
+    ref = oracle.c_attention_rows(q.astype(np.float16), k.astype(np.float16), x, 4096, 3072, cu,
+                                  rows, 1)
+    got = host_out[0].view(-1, 128)[torch.from_numpy(rows)].numpy().astype(np.float64)
+    assert np.abs(got - ref).max() <= 2e-3
