@@ -249,10 +249,15 @@ QWA_API qwa_status qwa_q40_dequantize(qwa_ctx *ctx, const void *packed, int n, i
                                       void *weight, void *stream);
 
 /* QuantMatmulKernel.createRunFromBuffers(input, weights, m, n, k, output) +
- * encode for the prepacked tile32 layout (quant-matmul.ts:495-540): the
- * first call for a given (packed, n, k) dequantises the matrix into an f16
- * copy owned by the context (n * k * 2 bytes, kept until qwa_q40_forget or
- * qwa_destroy); every call then runs qwa_matmul on that copy. The copy is
+ * encode for the prepacked tile32 layout (quant-matmul.ts:495-540). Like the
+ * reference, the pipeline depends on m (quant-matmul.ts:508): for m <= 64 and
+ * n <= 2048 the kernel reads the 20-byte records directly (dequantised in
+ * shared memory, K split over CTAs, partial sums in a context workspace of
+ * up to 16 * m * n floats that grows on first use; make one call of a shape
+ * before capturing it); otherwise the first call for a given (packed, n, k)
+ * dequantises the matrix into an f16 copy owned by the context (n * k * 2
+ * bytes, kept until qwa_q40_forget or qwa_destroy) and every call runs
+ * qwa_matmul on that copy. The copy is
  * found by the packed buffer's address: a caller that rewrites the packed
  * buffer in place, or frees it (the address may later hold another matrix),
  * calls qwa_q40_forget first. */

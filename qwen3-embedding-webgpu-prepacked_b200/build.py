@@ -14,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libqwa.so")
-SOURCES = ["api.cu", "attention.cu", "prologue.cu", "noalloc.cu", "pool.cu", "rmsnorm.cu", "gemm.cu", "q40.cu", "ffn.cu"]
+SOURCES = ["api.cu", "attention.cu", "prologue.cu", "noalloc.cu", "pool.cu", "rmsnorm.cu", "gemm.cu", "q40.cu", "ffn.cu", "q40_small.cu"]
 HEADERS = ["ptx.cuh", "internal.h", "attn_common.cuh", os.path.join("..", "..", "include", "qwa.h")]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -67,6 +67,8 @@ struct qwa_ctx {
   unsigned long long* trace = nullptr;           // QWA_TRACE builds only
   unsigned long long wait_ns = kWaitTimeoutNs;    // bounded-wait limit of the attention kernel
   int skip_load = -1;                             // test hook, see qwa_set_debug
+  float* small_ws = nullptr;                      // partial sums of the small-M Q4_0 path
+  size_t small_ws_bytes = 0;
 };
 
 namespace {
@@ -481,6 +483,7 @@ qwa_status qwa_destroy(qwa_ctx* ctx) {
     ctx->retired.clear();
     if (ctx->d_rope) cudaFree(ctx->d_rope);
     if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->small_ws) cudaFree(ctx->small_ws);
   }
   delete ctx;
   return QWA_OK;
@@ -577,6 +580,39 @@ qwa_status run_matmul(qwa_ctx* ctx, const void* input, const void* weight, void*
   if ((st = make_map_2d(ctx, &tm_out, output, n, m, 32)) != QWA_OK) return st;
   QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
                                 ctx->d_status, pair, stream));
+  return QWA_OK;
+}
+
+// Small batches (m <= 64 rows): the Q4_0 records are read directly (no f16
+// copy), K split across CTAs, partial sums in a context workspace.
+qwa_status run_q40_small(qwa_ctx* ctx, const void* input, const void* packed, void* output, int m,
+                         int n, int k, cudaStream_t stream) {
+  if (!input || !output) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(input) || !aligned16(output))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  qwa_status st = ensure_encode(ctx);
+  if (st != QWA_OK) return st;
+  const int splits = q40_small_splits(n, k, ctx->sms);
+  const size_t need = sizeof(float) * static_cast<size_t>(splits) * m * n;
+  if (need > ctx->small_ws_bytes) {
+    // grows once per larger shape; synchronises (cudaFree) outside any capture
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+      return fail(ctx, QWA_ERR_UNSUPPORTED,
+                  "the small-batch Q4_0 workspace must grow: make one call of this shape "
+                  "before capturing");
+    if (ctx->small_ws) cudaFree(ctx->small_ws);
+    ctx->small_ws = nullptr;
+    ctx->small_ws_bytes = 0;
+    QWA_CUDA(ctx, cudaMalloc(&ctx->small_ws, need));
+    ctx->small_ws_bytes = need;
+  }
+  CUtensorMap tm_x;
+  const uint32_t mpad = static_cast<uint32_t>((m + 15) / 16 * 16);
+  if ((st = make_map_2d(ctx, &tm_x, input, k, m, mpad)) != QWA_OK) return st;
+  QWA_CUDA(ctx, launch_q40_small_gemm(tm_x, static_cast<const uint8_t*>(packed),
+                                      static_cast<__half*>(output), m, n, k, splits,
+                                      ctx->small_ws, ctx->d_status, stream));
   return QWA_OK;
 }
 
@@ -730,9 +766,15 @@ qwa_status qwa_q40_matmul(qwa_ctx* ctx, const void* input, const void* packed, v
   qwa_status st = check_matmul_shape(ctx, m, n, k);
   if (st == QWA_OK) st = check_q40(ctx, packed, n, k);
   if (st != QWA_OK) return st;
+  if (m == 0) return QWA_OK;
+  // Few rows on a matrix of few output rows: the records are read directly
+  // (measured 1.5-1.9x faster than the f16 GEMM at n = 1024, k = 2048 / 3072;
+  // on par or slower for n = 4096 / 6144, where the f16 GEMM keeps enough CTAs
+  // busy without splitting K).
+  if (m <= kQ40SmallMaxRows && n <= 2048)
+    return run_q40_small(ctx, input, packed, output, m, n, k, s);
   __half* w = nullptr;
   if ((st = cached_q40(ctx, packed, n, k, s, &w)) != QWA_OK) return st;
-  if (m == 0) return QWA_OK;
   return run_matmul(ctx, input, w, output, m, n, k, s);
 }
 

@@ -193,6 +193,15 @@ cudaError_t launch_rms_norm(__half* x, const __half* residual, const float* weig
                             __half* normalized, int rows, int width, bool has_residual, float eps,
                             cudaStream_t stream);
 
+// Small-M projection from Q4_0 tile32 records (m <= kQ40SmallMaxRows, n % 128
+// == 0, k % 64 == 0): tm_x is the 2-D map of A {k, m} with box {64, m padded
+// to 16}; ws holds splits * m * n floats of partial sums.
+constexpr int kQ40SmallMaxRows = 64;
+int q40_small_splits(int n, int k, int sms);
+cudaError_t launch_q40_small_gemm(const CUtensorMap& tm_x, const uint8_t* packed, __half* out,
+                                  int m, int n, int k, int splits, float* ws, int* status,
+                                  cudaStream_t stream);
+
 // SwiGLU: out[r, c] = f16(silu(g) * u), g = combined[r, c], u = combined[r, width + c].
 cudaError_t launch_swiglu(const __half* combined, __half* out, int rows, int width,
                           cudaStream_t stream);

@@ -28,6 +28,7 @@ enum DeviceError : int {
   kDevTimeoutAccEmpty = 0x203,
   kDevTimeoutAccFull = 0x204,
   kDevTimeoutPairSync = 0x205,
+  kDevTimeoutSmallGemm = 0x301,
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

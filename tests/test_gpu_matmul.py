@@ -155,3 +155,30 @@ def test_q40_cache_entry_dies_with_its_tensor(pkg, cuda_dev):
                q40.matmul(a.cpu().numpy(), q40.dequant_tile32(packed, n, k)))
         del run, dp
         gc.collect()
+
+
+@pytest.mark.parametrize("m", [1, 7, 16, 33, 50, 64])
+@pytest.mark.parametrize("n,k", [(1024, 2048), (1024, 3072), (256, 1024), (2048, 64)])
+def test_q40_small_batch_reads_packed_records(pkg, cuda_dev, m, n, k):
+    """m <= 64 rows on n <= 2048: the projection reads the Q4_0 records
+    directly (K split over CTAs, partial sums added in a fixed order): oracle
+    parity, identical bits on a repeat, and a rewritten packed buffer is used
+    at once (no f16 copy is cached on this path)."""
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(m * 7 + n + k)
+    packed = _packed(rng, n, k)
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    kern = mm.QuantMatmulKernel(0)
+    dp = torch.from_numpy(packed).cuda()
+    run = kern.create_run_from_buffers(torch.from_numpy(a).cuda(), dp, m, n, k)
+    kern.encode(None, run)
+    first = run.output.clone()
+    kern.encode(None, run)
+    pkg.attention.Context.for_device(0).check()
+    assert torch.equal(first, run.output)
+    _check(first.cpu().numpy(), q40.matmul(a, q40.dequant_tile32(packed, n, k)))
+    packed2 = _packed(rng, n, k)
+    dp.copy_(torch.from_numpy(packed2))
+    kern.encode(None, run)
+    pkg.attention.Context.for_device(0).check()
+    _check(run.output.cpu().numpy(), q40.matmul(a, q40.dequant_tile32(packed2, n, k)))
