@@ -114,6 +114,17 @@ def q40_dequantize(packed: torch.Tensor, n: int, k: int, out: Optional[torch.Ten
     return out
 
 
+def q40_matmul(input: torch.Tensor, packed: torch.Tensor, n: int, k: int,
+               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """f16 [m, n] = input [m, k] @ W^T with W the Q4_0 tile32 matrix ``packed``
+    (quant-matmul.ts:495-540): m <= 64 rows on n <= 2048 read the records
+    directly; other shapes use the context's cached f16 copy."""
+    kern = QuantMatmulKernel(input.device.index)
+    run = kern.create_run_from_buffers(input, packed, input.shape[0], n, k, out)
+    kern.encode(stream, run)
+    return run.output
+
+
 def matmul(input: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor] = None,
            stream=None) -> torch.Tensor:
     """f16 [m, n] = input [m, k] @ weight [n, k]^T on the tensor cores."""

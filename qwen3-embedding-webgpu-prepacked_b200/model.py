@@ -34,6 +34,9 @@ from .pooling import last_token_pool
 
 HIDDEN, INTERMEDIATE, Q_WIDTH, LAYERS = 1024, 3072, 2048, 28  # model.ts:18-21
 EPSILON = 1e-6
+# batches of at most this many tokens run the 1024-row projections (attn_output,
+# ffn_down) straight from the Q4_0 records (qwa_q40_matmul's small-batch path)
+SMALL_ROWS = 64
 
 # name -> [k, n] of each compact Q4_0 matrix of a block (model.ts:89-101)
 COMPACT = {"attn_qkv": [HIDDEN, 4096], "attn_output": [Q_WIDTH, HIDDEN],
@@ -95,6 +98,7 @@ class Qwen3EmbeddingModel:
         self.vocab = int(emb_dims[1])
         self.embed_table = weights.weight("token_embd.weight")
         self.f16 = []  # per layer: dequantised projections, f16 [n, k]
+        self.packed = []  # per layer: the compact Q4_0 bytes of attn_output / ffn_down
         self.gains = []
         for l in range(self.layers):
             mats = {}
@@ -105,6 +109,8 @@ class Qwen3EmbeddingModel:
                 k, n = kn
                 mats[name] = matmul.q40_dequantize(weights.weight(full), n, k)
             self.f16.append(mats)
+            self.packed.append({name: weights.weight(f"blk.{l}.{name}.weight")
+                                for name in ("attn_output", "ffn_down")})
             self.gains.append({key: weights.weight(f"blk.{l}.{key}.weight").float().contiguous()
                                for key in ("attn_norm", "attn_q_norm", "attn_k_norm",
                                            "ffn_norm")})
@@ -133,11 +139,19 @@ class Qwen3EmbeddingModel:
                                   cu_seqlens, EPSILON, q_out=q, k_out=k, v_out=v)
             attn.attention(q, k, v, cu_seqlens, value_stride=1024, value_offset=0, mode=mode,
                            out=o)
-            matmul.matmul(o.view(T, Q_WIDTH), w["attn_output"], out=delta)
+            if T <= SMALL_ROWS:  # few rows: read the Q4_0 records (less weight traffic)
+                matmul.q40_matmul(o.view(T, Q_WIDTH), self.packed[l]["attn_output"], HIDDEN,
+                                  Q_WIDTH, out=delta)
+            else:
+                matmul.matmul(o.view(T, Q_WIDTH), w["attn_output"], out=delta)
             norm.rms_norm(x, g["ffn_norm"], residual=delta, out=normalized)
             matmul.matmul(normalized, w["ffn_gate_up"], out=gate_up)
             ffn.swiglu(gate_up, INTERMEDIATE, out=hidden)
-            matmul.matmul(hidden, w["ffn_down"], out=delta)
+            if T <= SMALL_ROWS:
+                matmul.q40_matmul(hidden, self.packed[l]["ffn_down"], HIDDEN, INTERMEDIATE,
+                                  out=delta)
+            else:
+                matmul.matmul(hidden, w["ffn_down"], out=delta)
             nxt = self.gains[l + 1]["attn_norm"] if l + 1 < self.layers else self.output_norm
             norm.rms_norm(x, nxt, residual=delta, out=normalized)
             if trace is not None:
