@@ -172,3 +172,87 @@ class Qwen3EmbeddingModel:
     def create_varlen_plan(self, batch: int, capacity: int):
         from .engine import _VarlenPlan
         return _VarlenPlan(self, batch, capacity)
+
+
+class MultiDeviceModel:
+    """One micro-batch of embedding requests over several devices of a box:
+    each device holds its own ``Qwen3EmbeddingModel`` (weights replicated),
+    the requests are split by LPT on their attention work
+    (``sharding.lpt_shard``), every device runs its share as one packed batch
+    from one host thread, and the embeddings come back in request order. No
+    collective is involved. AUTO attention is resolved on the whole
+    micro-batch, as one device would (ops.ts:328).
+
+    It offers the engine's runtime interface (``create_plan`` /
+    ``create_varlen_plan``), so ``EmbeddingEngine`` can drive it unchanged."""
+
+    hidden = HIDDEN
+
+    def __init__(self, models: Sequence[Qwen3EmbeddingModel]):
+        if not models:
+            raise ValueError("models must not be empty")
+        self.models = list(models)
+
+    def embed_packed(self, ids: np.ndarray, cu_seqlens: Sequence[int],
+                     mode: int = attn.MODE_AUTO) -> np.ndarray:
+        """f32 [batch, 1024] embeddings of packed host ids (int)."""
+        import threading
+
+        from . import sharding
+        cu = [int(c) for c in cu_seqlens]
+        lengths = [cu[b + 1] - cu[b] for b in range(len(cu) - 1)]
+        sparse = sharding.resolve_sparse(mode, lengths)
+        rmode = attn.MODE_SPARSE if sparse else attn.MODE_FULL
+        assignment = sharding.lpt_shard(lengths, len(self.models), rmode)
+        out = np.zeros((len(lengths), HIDDEN), np.float32)
+        errors: List[BaseException] = []
+
+        def work(r: int) -> None:
+            reqs = [b for b in assignment[r] if lengths[b] > 0]
+            if not reqs:
+                return
+            try:
+                m = self.models[r]
+                local_ids = np.concatenate([ids[cu[b]:cu[b + 1]] for b in reqs])
+                local_cu = [0] + np.cumsum([lengths[b] for b in reqs]).astype(int).tolist()
+                with torch.cuda.device(m.device):
+                    d_ids = torch.from_numpy(local_ids.astype(np.int32)).to(m.device)
+                    emb = last_token_pool(m.forward(d_ids, local_cu, rmode), local_cu)
+                    out[reqs] = emb.cpu().numpy()
+            except BaseException as e:  # noqa: BLE001 -- re-raised on the caller's thread
+                errors.append(e)
+
+        threads = [threading.Thread(target=work, args=(r,)) for r in range(len(self.models))]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+        return out
+
+    def create_plan(self, batch: int, sequence: int):
+        return _MultiPlan(self, batch, sequence)
+
+    def create_varlen_plan(self, batch: int, capacity: int):
+        return _MultiPlan(self, batch, capacity)
+
+
+class _MultiPlan:
+    """Both packings reduce to the packed batch of the requests' own tokens
+    (a padded plan's EOS padding never changes a request's last-token
+    embedding, since attention is causal)."""
+
+    def __init__(self, rt: MultiDeviceModel, batch: int, size: int):
+        self.rt, self.batch, self.size = rt, batch, size
+
+    def run(self, ids: np.ndarray, lengths: np.ndarray) -> List[np.ndarray]:
+        seq = self.size
+        packed = np.concatenate([ids[b * seq:b * seq + int(n)] for b, n in enumerate(lengths)])
+        cu = [0] + np.cumsum(np.asarray(lengths, int)).tolist()
+        return list(self.rt.embed_packed(packed, cu))
+
+    def run_varlen(self, ids: np.ndarray, cu_seqlens: np.ndarray) -> List[np.ndarray]:
+        if int(cu_seqlens[-1]) > self.size:
+            raise ValueError("micro-batch exceeds the plan's token capacity")
+        return list(self.rt.embed_packed(np.asarray(ids), cu_seqlens))

@@ -141,3 +141,24 @@ def test_small_batch_model_against_oracle(pkg, cuda_dev, synthetic_model):
     cos = float((emb.cpu().numpy().astype(np.float64) * ref).sum())
     print("MODEL_SMALL embedding cosine", cos)
     assert cos >= 0.9999
+
+
+def test_multi_device_model_through_the_engine(pkg, cuda_dev, synthetic_model):
+    """The model replicated on two devices (both cuda:0 here; two host
+    threads), requests split between them: the engine's embeddings equal the
+    single-device ones within the batch-vs-single gate."""
+    eng_mod = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.engine")
+    parsed, model = synthetic_model
+    second = pkg.model.Qwen3EmbeddingModel(pkg.prepacked.PrepackedWeights(parsed, 0))
+    multi = pkg.model.MultiDeviceModel([model, second])
+    rng = np.random.default_rng(6)
+    reqs = [list(rng.integers(0, 4095, size=n - 1)) + [4095] for n in (300, 700, 5, 150, 90)]
+
+    async def embed_all(rt, packing):
+        eng = eng_mod.EmbeddingEngine(rt, None, 16, 0, 4095, packing=packing)
+        return await asyncio.gather(*[eng.submit_tokens(r) for r in reqs])
+
+    one = np.stack(asyncio.run(embed_all(model, "varlen")))
+    for packing in ("varlen", "padded"):
+        two = np.stack(asyncio.run(embed_all(multi, packing)))
+        assert np.sum(one * two, axis=1).min() >= 0.9999
