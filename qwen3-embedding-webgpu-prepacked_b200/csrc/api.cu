@@ -110,10 +110,10 @@ qwa_status ensure_encode(qwa_ctx* ctx) {
 // row_stride_bytes; box {64, 1, 128} with 128-byte swizzle, so one load
 // lands as 128 rows x 128 B (the canonical SW128 K-major atom layout).
 qwa_status make_map(qwa_ctx* ctx, CUtensorMap* map, const void* base, int heads, int64_t rows,
-                    int64_t row_stride_bytes) {
+                    int64_t row_stride_bytes, uint32_t box_rows = 128) {
   cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(row_stride_bytes)};
-  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t box[3] = {64, 1, box_rows};
   cuuint32_t elem[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
                         strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -408,7 +408,7 @@ qwa_status run_attention(qwa_ctx* ctx, const void* q, const void* k, const void*
   if (st != QWA_OK) return st;
   CUtensorMap tm_q, tm_k, tm_v, tm_o;
   if ((st = make_map(ctx, &tm_q, q, kQHeads, total, kQHeads * kHeadDim * 2)) != QWA_OK) return st;
-  if ((st = make_map(ctx, &tm_o, out, kQHeads, total, kQHeads * kHeadDim * 2)) != QWA_OK) return st;
+  if ((st = make_map(ctx, &tm_o, out, kQHeads, total, kQHeads * kHeadDim * 2, kOutBoxRows)) != QWA_OK) return st;
   if ((st = make_map(ctx, &tm_k, k, kKVHeads, total, kKVHeads * kHeadDim * 2)) != QWA_OK) return st;
   if ((st = make_map(ctx, &tm_v, v_base, kKVHeads, total, v_stride * 2)) != QWA_OK) return st;
   AttnArgs args;

@@ -119,6 +119,9 @@ __device__ __forceinline__ ItemRange item_range(const AttnArgs& a, int num_items
 // Timeline layout of a QWA_TRACE build: trace[(cta * kTraceEvents + event) *
 // kTraceIters + key_tile] = clock64() for the first kTraceCtas CTAs (key_tile
 // counts the CTA's tiles across its work items).
+// Rows of one TMA box of the attention output map tm_o.
+constexpr int kOutBoxRows = 32;
+
 constexpr int kTraceCtas = 4;
 constexpr int kTraceEvents = 69;
 constexpr int kTraceIters = 256;

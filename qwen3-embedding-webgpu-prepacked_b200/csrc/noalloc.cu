@@ -145,10 +145,11 @@ qwa_status setup_device(int device, unsigned char** out) {
   return QWA_OK;
 }
 
-bool map3d(CUtensorMap* map, const void* base, int heads, int64_t rows, int64_t row_stride) {
+bool map3d(CUtensorMap* map, const void* base, int heads, int64_t rows, int64_t row_stride,
+           uint32_t box_rows = 128) {
   cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[2] = {256, static_cast<cuuint64_t>(row_stride)};
-  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t box[3] = {64, 1, box_rows};
   cuuint32_t elem[3] = {1, 1, 1};
   return g_encode_na(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims,
                      strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -210,7 +211,7 @@ extern "C" qwa_status qwa_attention_noalloc(const void* q, const void* k, const 
 
   CUtensorMap tm_q, tm_k, tm_v, tm_o;
   if (!map3d(&tm_q, q, kQHeads, total, kQHeads * kHeadDim * 2) ||
-      !map3d(&tm_o, out, kQHeads, total, kQHeads * kHeadDim * 2) ||
+      !map3d(&tm_o, out, kQHeads, total, kQHeads * kHeadDim * 2, kOutBoxRows) ||
       !map3d(&tm_k, k, kKVHeads, total, kKVHeads * kHeadDim * 2) ||
       !map3d(&tm_v, v_base, kKVHeads, total, v_stride * 2))
     return QWA_ERR_CUDA;
