@@ -53,9 +53,9 @@ enum TraceEvent : int {
   kTrMmaPVAHiDone, kTrMmaSADone,
   kTrWarpMax,             // +softmax warp (0..7): lane 0 after the row max
   kTrWarpArrive = kTrWarpMax + 8,   // +softmax warp: lane 0 at its P-hi arrival
-  kTrEpiChunk = kTrWarpArrive + 8,  // +X*4+c: reserved (warpgroup-staged epilogue)
-  kTrEpiStaged = kTrEpiChunk + 8,   // +X: reserved
-  kTrEpiIssued = kTrEpiStaged + 2,  // +X: reserved
+  kTrEpiChunk = kTrWarpArrive + 8,  // CTA entry/exit: [0]/[1] globaltimer, [2]/[3] clock64
+  kTrEpiStaged = kTrEpiChunk + 8,   // issuer: +0 before / +1 after its Q wait (first tile t)
+  kTrEpiIssued = kTrEpiStaged + 2,  // producer: +0 Q load issued (item li)
   kTrWarpEpi = kTrEpiIssued + 2,    // +softmax warp: lane 0 past the O-final wait
   kTrWarpStaged = kTrWarpEpi + 8    // +softmax warp: lane 0 at its staged arrival
 };
@@ -156,6 +156,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+#ifdef QWA_TRACE
+  if (threadIdx.x == 0 && args.trace && blockIdx.x < kTraceCtas) {
+    args.trace[(blockIdx.x * kTraceEvents + kTrEpiChunk) * kTraceIters + 0] = globaltimer();
+    args.trace[(blockIdx.x * kTraceEvents + kTrEpiChunk) * kTraceIters + 2] = clock64();
+  }
+#endif
 
   // Work items of this CTA: its own list from the plan's schedule (longest
   // first), or blockIdx.x, blockIdx.x + gridDim.x, ... without one. li counts
@@ -185,6 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = mbar_wait(bar(kQEmpty + qb), ((li >> 1) & 1) ^ 1, abort_flag, args.status,
                              kDevTimeoutQ, wait_limit)))
           break;
+        QWA_TR(kTrEpiIssued + 0, li);
         mbar_arrive_expect_tx(bar(kQFull + qb), kQBufBytes);
         issued = (issued & ~(1u << (kSlots + qb))) | (1u << (kSlots + qb + 8)) |
                  (static_cast<uint32_t>((li >> 1) & 1) << (kSlots + qb));
@@ -256,9 +263,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qb = li & 1;
         const uint64_t qa = q_desc0 + ((qb * kQBufBytes) >> 4);
         const uint64_t qbd = qa + (kTileBytes >> 4);
+        QWA_TR(kTrEpiStaged + 0, t);
         if (!(ok = mbar_wait(bar(kQFull + qb), (li >> 1) & 1, abort_flag, args.status,
                              kDevTimeoutQ, wait_limit)))
           break;
+        QWA_TR(kTrEpiStaged + 1, t);
         for (int j = 0; j < sch.n; ++j, ++t) {
           const int ck = 2 * t, sk = ck % kSlots;
           const int cv = 2 * t + 1, sv = cv % kSlots;
@@ -559,6 +568,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   bulk_wait_all();  // epilogue stores of the last items (no-op for other threads)
   tc_fence_before();
   __syncthreads();
+#ifdef QWA_TRACE
+  if (threadIdx.x == 0 && args.trace && blockIdx.x < kTraceCtas) {
+    args.trace[(blockIdx.x * kTraceEvents + kTrEpiChunk) * kTraceIters + 1] = globaltimer();
+    args.trace[(blockIdx.x * kTraceEvents + kTrEpiChunk) * kTraceIters + 3] = clock64();
+  }
+#endif
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);

@@ -76,23 +76,10 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&a)[32], int k0, int q, int
   if (sparse) m &= low_bits(prefix - k0) | ~low_bits(q - window + 1 - k0);
   // The window and causal edges are diagonals: a warp's 32 rows cut at most
   // two of a tile's four chunks, and the others need no per-element work.
-#ifdef QWA_MASK3
-  if (!__all_sync(0xffffffffu, m == 0xffffffffu)) {
-    if (__all_sync(0xffffffffu, m == 0u)) {
-#pragma unroll
-      for (int c = 0; c < 32; ++c) a[c] = __float_as_uint(-INFINITY);
-    } else {
-#pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (!((m >> c) & 1u)) a[c] = __float_as_uint(-INFINITY);
-    }
-  }
-#else
   if (__all_sync(0xffffffffu, m == 0xffffffffu)) return;
 #pragma unroll
   for (int c = 0; c < 32; ++c)
     if (!((m >> c) & 1u)) a[c] = __float_as_uint(-INFINITY);
-#endif
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {

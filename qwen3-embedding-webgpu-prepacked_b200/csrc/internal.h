@@ -122,7 +122,11 @@ __device__ __forceinline__ ItemRange item_range(const AttnArgs& a, int num_items
 // Rows of one TMA box of the attention output map tm_o.
 constexpr int kOutBoxRows = 32;
 
+#ifdef QWA_TRACE_ALL_CTAS
+constexpr int kTraceCtas = 148;
+#else
 constexpr int kTraceCtas = 4;
+#endif
 constexpr int kTraceEvents = 69;
 constexpr int kTraceIters = 256;
 
