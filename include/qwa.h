@@ -240,6 +240,17 @@ QWA_API qwa_status qwa_embedding_lookup_q6k(qwa_ctx *ctx, const uint32_t *ids_de
 QWA_API qwa_status qwa_matmul(qwa_ctx *ctx, const void *input, const void *weight, void *output,
                               int m, int n, int k, void *stream);
 
+/* ffn_gate_up projection fused with the FFN's SwiGLU (model.ts:98-100 with
+ * SwiGLUKernel, ops.ts:74-102): output f16 [m, n/2] with
+ *   output[r, c] = f16(g / (1 + exp(-g)) * u),  g = f16(gate[r, c]), u = f16(up[r, c]),
+ * bit for bit what qwa_matmul followed by qwa_swiglu gives. weight f16 [n, k]
+ * holds the gate_up matrix with its rows interleaved in blocks of 128: rows
+ * 256b..256b+127 are gate rows 128b.., rows 256b+128..256b+255 up rows 128b..
+ * (the reference's layout is gate rows 0..n/2-1, then up rows). n a multiple
+ * of 256, k of 64. */
+QWA_API qwa_status qwa_matmul_swiglu(qwa_ctx *ctx, const void *input, const void *weight,
+                                     void *output, int m, int n, int k, void *stream);
+
 /* Dequantise a Q4_0 "q4_0-tile32-compact" matrix (src/prepacked/format.ts:
  * 65-99; values as quant-matmul.ts:98-107, f16(scale) * (q - 8) in f16) to
  * f16 weight[n, k] row-major. packed: ceil(n/32) * (k/32) * 32 records of 20

@@ -39,6 +39,7 @@ SIGNATURES = {
     "qwa_selftest_tile": (I32, [P, P, P, P, P, P, P]),
     "qwa_attention_noalloc": (I32, [P, P, P, I64, I64, P, I32P, I32, I32, I32, I32, P]),
     "qwa_matmul": (I32, [P, P, P, P, I32, I32, I32, P]),
+    "qwa_matmul_swiglu": (I32, [P, P, P, P, I32, I32, I32, P]),
     "qwa_q40_dequantize": (I32, [P, P, I32, I32, P, P]),
     "qwa_q40_matmul": (I32, [P, P, P, P, I32, I32, I32, P]),
     "qwa_q40_forget": (I32, [P, P]),

@@ -641,6 +641,27 @@ qwa_status qwa_q40_dequantize(qwa_ctx* ctx, const void* packed, int n, int k, vo
   return QWA_OK;
 }
 
+qwa_status qwa_matmul_swiglu(qwa_ctx* ctx, const void* input, const void* weight, void* output,
+                             int m, int n, int k, void* stream) {
+  if (!ctx) return QWA_ERR_INVALID_ARG;
+  DeviceGuard guard(ctx->device);
+  qwa_status st = check_matmul_shape(ctx, m, n, k);
+  if (st != QWA_OK) return st;
+  if (m == 0) return QWA_OK;
+  if (!input || !weight || !output) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
+  if (!aligned16(input) || !aligned16(weight) || !aligned16(output))
+    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
+  if ((st = ensure_encode(ctx)) != QWA_OK) return st;
+  const bool pair = gemm_pair(m);
+  CUtensorMap tm_a, tm_w, tm_out;
+  if ((st = make_map_2d(ctx, &tm_a, input, k, m, 128)) != QWA_OK) return st;
+  if ((st = make_map_2d(ctx, &tm_w, weight, k, n, kGemmWBoxRows(pair))) != QWA_OK) return st;
+  if ((st = make_map_2d(ctx, &tm_out, output, n / 2, m, 32)) != QWA_OK) return st;
+  QWA_CUDA(ctx, launch_gemm_glu(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
+                                ctx->d_status, pair, static_cast<cudaStream_t>(stream)));
+  return QWA_OK;
+}
+
 qwa_status qwa_matmul(qwa_ctx* ctx, const void* input, const void* weight, void* output, int m,
                       int n, int k, void* stream) {
   if (!ctx) return QWA_ERR_INVALID_ARG;

@@ -201,7 +201,7 @@ __device__ __forceinline__ void norm_rope_quarter(uint32_t t_tile, int c, int su
   }
 }
 
-template <bool kQkv, bool kPair>
+template <bool kQkv, bool kPair, bool kGlu = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_a,
                     const __grid_constant__ CUtensorMap tm_w,
@@ -372,7 +372,75 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t t_tile = tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * kBN;
       const uint32_t t_cols = t_tile + 128 * half;
-      if (kQkv && nt < 12) {
+      if constexpr (kGlu) {
+        // Fused SwiGLU (gate_up weight rows interleaved in 128-row blocks):
+        // tile columns 0..127 are gate values g, 128..255 the up values u of
+        // the same 128 outputs. Warp half h produces outputs [64h, 64h + 64):
+        // f16(g / (1 + exp(-g)) * u) with g and u first rounded to f16, as
+        // the unfused GEMM stores them and swiglu_kernel reads them.
+        const int oc = nt * 128 + 64 * half;  // output column in [M, N / 2]
+        auto glu_pack = [&](const uint32_t (&g)[32], const uint32_t (&u)[32], int i) {
+          const float g0 = f16_round(__uint_as_float(g[2 * i]));
+          const float g1 = f16_round(__uint_as_float(g[2 * i + 1]));
+          const float u0 = f16_round(__uint_as_float(u[2 * i]));
+          const float u1 = f16_round(__uint_as_float(u[2 * i + 1]));
+          const float s0 = g0 / (1.0f + expf(-g0));
+          const float s1 = g1 / (1.0f + expf(-g1));
+          return pack_half2(s0 * u0, s1 * u1);
+        };
+        if constexpr (L::kTmaOut) {
+          const uint32_t stage = sbase + L::kOutOff + (warp - 2) * 4096;
+          if (lane == 0) bulk_wait_read();  // the previous store has read the buffer
+          __syncwarp();
+#pragma unroll 1
+          for (int b = 0; b < 2; ++b) {
+            uint32_t g[32], u[32];
+            tmem_ld32(t_tile + 64 * half + 32 * b, g);
+            tmem_ld32(t_tile + 128 + 64 * half + 32 * b, u);
+            tmem_wait_ld();
+            reg_fence32(g);
+            reg_fence32(u);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint32_t w0 = glu_pack(g, u, 4 * q + 0), w1 = glu_pack(g, u, 4 * q + 1);
+              const uint32_t w2 = glu_pack(g, u, 4 * q + 2), w3 = glu_pack(g, u, 4 * q + 3);
+              const uint32_t unit = static_cast<uint32_t>(4 * b + q);
+              const uint32_t addr = stage + lane * 128 + ((unit ^ (lane & 7)) << 4);
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w0),
+                           "r"(w1), "r"(w2), "r"(w3)
+                           : "memory");
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_out, stage, oc, m0 + sub * 32);  // rows >= M are clipped
+            bulk_commit();
+          }
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * (N / 2) + oc);
+#pragma unroll 1
+          for (int b = 0; b < 2; ++b) {
+            uint32_t g[32], u[32];
+            tmem_ld32(t_tile + 64 * half + 32 * b, g);
+            tmem_ld32(t_tile + 128 + 64 * half + 32 * b, u);
+            tmem_wait_ld();
+            reg_fence32(g);
+            reg_fence32(u);
+            if (row < M) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 wv;
+                wv.x = glu_pack(g, u, 4 * q + 0);
+                wv.y = glu_pack(g, u, 4 * q + 1);
+                wv.z = glu_pack(g, u, 4 * q + 2);
+                wv.w = glu_pack(g, u, 4 * q + 3);
+                dst[4 * b + q] = wv;
+              }
+            }
+          }
+        }
+      } else if (kQkv && nt < 12) {
         // q tiles 0..7 (heads 2nt, 2nt+1), k tiles 8..11 (kv heads 2(nt-8), +1)
         const bool is_q = nt < 8;
         const int head0 = is_q ? 2 * nt : 2 * (nt - 8);
@@ -492,7 +560,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-template <bool kQkv, bool kPair>
+template <bool kQkv, bool kPair, bool kGlu = false>
 cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
                         const CUtensorMap& tm_out, const CUtensorMap& tm_qo,
                         const CUtensorMap& tm_ko, __half* out, int M, int N, int K, int* status,
@@ -505,7 +573,7 @@ cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_f16_kernel<kQkv, kPair>,
+    e = cudaFuncSetAttribute(gemm_f16_kernel<kQkv, kPair, kGlu>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem);
     if (e == cudaSuccess)
       e = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
@@ -529,11 +597,11 @@ cudaError_t launch_gemm(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair>, tm_a, tm_w, tm_out, tm_qo, tm_ko,
+    return cudaLaunchKernelEx(&cfg, gemm_f16_kernel<kQkv, kPair, kGlu>, tm_a, tm_w, tm_out, tm_qo, tm_ko,
                               out, M, N, K, status, qkv);
   }
   const int grid = tiles < sm_count[dev] ? tiles : sm_count[dev];
-  gemm_f16_kernel<kQkv, kPair><<<grid, kGemmThreads, L::kSmem, stream>>>(
+  gemm_f16_kernel<kQkv, kPair, kGlu><<<grid, kGemmThreads, L::kSmem, stream>>>(
       tm_a, tm_w, tm_out, tm_qo, tm_ko, out, M, N, K, status, qkv);
   return cudaGetLastError();
 }
@@ -548,6 +616,15 @@ cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
                                          QkvEpilogue{}, stream)
               : launch_gemm<false, false>(tm_a, tm_w, tm_out, tm_out, tm_out, out, M, N, K, status,
                                           QkvEpilogue{}, stream);
+}
+
+cudaError_t launch_gemm_glu(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                            const CUtensorMap& tm_out, __half* out, int M, int N, int K,
+                            int* status, bool pair, cudaStream_t stream) {
+  return pair ? launch_gemm<false, true, true>(tm_a, tm_w, tm_out, tm_out, tm_out, out, M, N, K,
+                                               status, QkvEpilogue{}, stream)
+              : launch_gemm<false, false, true>(tm_a, tm_w, tm_out, tm_out, tm_out, out, M, N, K,
+                                                status, QkvEpilogue{}, stream);
 }
 
 cudaError_t launch_gemm_qkv(const CUtensorMap& tm_a, const CUtensorMap& tm_w,

@@ -167,6 +167,12 @@ constexpr int kGemmPairMinRows = 4096;
 cudaError_t launch_gemm_f16(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
                             const CUtensorMap& tm_out, __half* out, int M, int N, int K,
                             int* status, bool pair, cudaStream_t stream);
+// The same GEMM with the FFN's SwiGLU in the epilogue: W's rows are the
+// gate_up matrix interleaved in 128-row blocks (gate block b, then up block
+// b), and the output is [M, N / 2] (tm_out: {N / 2, M}, box {64, 32}).
+cudaError_t launch_gemm_glu(const CUtensorMap& tm_a, const CUtensorMap& tm_w,
+                            const CUtensorMap& tm_out, __half* out, int M, int N, int K,
+                            int* status, bool pair, cudaStream_t stream);
 
 // Fused attn_qkv projection epilogue: per-head Q/K RMSNorm + RoPE on the q/k
 // tiles, v written as [T, 1024]. Positions are row - cu[request(row)].

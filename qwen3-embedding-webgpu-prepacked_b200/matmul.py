@@ -140,6 +140,32 @@ def matmul(input: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor
     return out
 
 
+def interleave_gate_up(weight: torch.Tensor) -> torch.Tensor:
+    """The gate_up weight [2w, k] (gate rows, then up rows) with its rows
+    interleaved in 128-row blocks, the layout ``matmul_swiglu`` reads."""
+    n, k = weight.shape
+    _need(n % 256 == 0, "gate_up rows must be a multiple of 256")
+    return weight.view(2, n // 256, 128, k).transpose(0, 1).reshape(n, k).contiguous()
+
+
+def matmul_swiglu(input: torch.Tensor, weight_interleaved: torch.Tensor,
+                  out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """f16 [m, n/2] = SwiGLU of input [m, k] @ gate_up^T, the SwiGLU applied in
+    the GEMM's epilogue (bit for bit ``swiglu(matmul(...))``); the weight is
+    ``interleave_gate_up(gate_up)``."""
+    m, k = input.shape
+    n = weight_interleaved.shape[0]
+    _f16(input, "input", m * k)
+    _f16(weight_interleaved, "weight", n * k)
+    out = out if out is not None else torch.empty(m, n // 2, dtype=torch.float16,
+                                                  device=input.device)
+    _f16(out, "out", m * (n // 2))
+    ctx = Context.for_device(input.device.index)
+    _lib.check(ctx.lib.qwa_matmul_swiglu(ctx.handle, _ptr(input), _ptr(weight_interleaved),
+                                         _ptr(out), m, n, k, _stream(stream)), ctx.handle)
+    return out
+
+
 def qkv_projection(input: torch.Tensor, weight: torch.Tensor, q_weight: torch.Tensor,
                    k_weight: torch.Tensor, cu_seqlens, eps: float = 1e-6, theta: float = 1e6,
                    q_out: Optional[torch.Tensor] = None, k_out: Optional[torch.Tensor] = None,

@@ -7,8 +7,9 @@ Follows ``Qwen3ExecutionPlan`` (src/webgpu/model.ts:60-136) step for step:
 * per layer: the attn_qkv projection (Q4_0) with the per-head Q/K RMSNorm +
   RoPE fused into its epilogue, attention (sparse 176 + 432 rule up to 8192
   tokens), the attn_output projection, residual + RMSNorm with ffn_norm, the
-  ffn_gate_up projection, SwiGLU, the ffn_down projection, and residual +
-  RMSNorm with the next layer's attn_norm (output_norm after the last);
+  ffn_gate_up projection with the SwiGLU in its epilogue, the ffn_down
+  projection, and residual + RMSNorm with the next layer's attn_norm
+  (output_norm after the last);
 * the last-token L2 pool of the final normalized state (ops.ts:347-379).
 
 Every step is a libqwa kernel. Projections run on the tcgen05 GEMM from f16
@@ -108,6 +109,9 @@ class Qwen3EmbeddingModel:
                     raise ValueError(f"{full} must be a compact Q4_0 matrix of dimensions {kn}")
                 k, n = kn
                 mats[name] = matmul.q40_dequantize(weights.weight(full), n, k)
+            # gate_up rows interleaved in 128-row blocks for the GEMM whose
+            # epilogue applies the SwiGLU (no [T, 6144] intermediate)
+            mats["ffn_gate_up"] = matmul.interleave_gate_up(mats["ffn_gate_up"])
             self.f16.append(mats)
             self.packed.append({name: weights.weight(f"blk.{l}.{name}.weight")
                                 for name in ("attn_output", "ffn_down")})
@@ -127,7 +131,6 @@ class Qwen3EmbeddingModel:
         x = ffn.embedding_lookup(ids, self.embed_table, HIDDEN, self.vocab)
         normalized = norm.rms_norm(x, self.gains[0]["attn_norm"])
         delta = torch.empty(T, HIDDEN, **f16)
-        gate_up = torch.empty(T, 2 * INTERMEDIATE, **f16)
         hidden = torch.empty(T, INTERMEDIATE, **f16)
         q = torch.empty(T, 16, 128, **f16)
         k = torch.empty(T, 8, 128, **f16)
@@ -145,8 +148,7 @@ class Qwen3EmbeddingModel:
             else:
                 matmul.matmul(o.view(T, Q_WIDTH), w["attn_output"], out=delta)
             norm.rms_norm(x, g["ffn_norm"], residual=delta, out=normalized)
-            matmul.matmul(normalized, w["ffn_gate_up"], out=gate_up)
-            ffn.swiglu(gate_up, INTERMEDIATE, out=hidden)
+            matmul.matmul_swiglu(normalized, w["ffn_gate_up"], out=hidden)
             if T <= SMALL_ROWS:
                 matmul.q40_matmul(hidden, self.packed[l]["ffn_down"], HIDDEN, INTERMEDIATE,
                                   out=delta)

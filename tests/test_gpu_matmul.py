@@ -88,6 +88,31 @@ def test_matmul_rejects_unsupported_shapes(pkg, cuda_dev):
                   torch.zeros(256, 40, dtype=torch.float16, device="cuda"))
 
 
+@pytest.mark.parametrize("m,n,k", [(197, 6144, 1024), (1, 512, 64), (4096, 6144, 1024),
+                                   (5000, 1024, 128), (64, 6144, 1024)])
+def test_gate_up_swiglu_equals_unfused_bits(pkg, cuda_dev, m, n, k):
+    """gate_up GEMM with the SwiGLU in its epilogue (interleaved weight rows)
+    must give the bits of the GEMM, its f16 output, then the SwiGLU kernel;
+    m = 4096 and 5000 take the CTA-pair shape with TMA stores."""
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    rng = np.random.default_rng(m + n + k)
+    x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float16)).cuda()
+    w = torch.from_numpy((rng.standard_normal((n, k)) * 2 * k ** -0.5).astype(np.float16)).cuda()
+    fused = mm.matmul_swiglu(x, mm.interleave_gate_up(w))
+    ref = pkg.ffn.swiglu(mm.matmul(x, w), n // 2)
+    pkg.attention.Context.for_device(0).check()
+    assert fused.shape == (m, n // 2)
+    assert torch.equal(fused.view(torch.int16), ref.view(torch.int16))
+
+
+def test_interleave_gate_up_layout(pkg):
+    mm = importlib.import_module("qwen3-embedding-webgpu-prepacked_b200.matmul")
+    w = torch.arange(512 * 2, dtype=torch.float32).view(512, 2).half()
+    il = mm.interleave_gate_up(w)
+    assert torch.equal(il[0:128], w[0:128]) and torch.equal(il[128:256], w[256:384])
+    assert torch.equal(il[256:384], w[128:256]) and torch.equal(il[384:512], w[384:512])
+
+
 @pytest.mark.parametrize("lengths,k", [([50, 17, 130], 1024), ([1], 64), ([5000, 128, 1], 1024),
                                        ([300, 0, 257], 2048)])
 def test_fused_qkv_projection_equals_unfused_bits(pkg, cuda_dev, lengths, k):
