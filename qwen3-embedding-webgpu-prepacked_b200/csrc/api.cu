@@ -566,8 +566,9 @@ qwa_status check_matmul_shape(qwa_ctx* ctx, int m, int n, int k) {
   return QWA_OK;
 }
 
+// glu: the gate_up form with the SwiGLU in the epilogue (output [m, n / 2]).
 qwa_status run_matmul(qwa_ctx* ctx, const void* input, const void* weight, void* output, int m,
-                      int n, int k, cudaStream_t stream) {
+                      int n, int k, cudaStream_t stream, bool glu = false) {
   if (!input || !weight || !output) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
   if (!aligned16(input) || !aligned16(weight) || !aligned16(output))
     return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
@@ -577,9 +578,13 @@ qwa_status run_matmul(qwa_ctx* ctx, const void* input, const void* weight, void*
   CUtensorMap tm_a, tm_w, tm_out;
   if ((st = make_map_2d(ctx, &tm_a, input, k, m, 128)) != QWA_OK) return st;
   if ((st = make_map_2d(ctx, &tm_w, weight, k, n, kGemmWBoxRows(pair))) != QWA_OK) return st;
-  if ((st = make_map_2d(ctx, &tm_out, output, n, m, 32)) != QWA_OK) return st;
-  QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
-                                ctx->d_status, pair, stream));
+  if ((st = make_map_2d(ctx, &tm_out, output, glu ? n / 2 : n, m, 32)) != QWA_OK) return st;
+  if (glu)
+    QWA_CUDA(ctx, launch_gemm_glu(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
+                                  ctx->d_status, pair, stream));
+  else
+    QWA_CUDA(ctx, launch_gemm_f16(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
+                                  ctx->d_status, pair, stream));
   return QWA_OK;
 }
 
@@ -648,18 +653,7 @@ qwa_status qwa_matmul_swiglu(qwa_ctx* ctx, const void* input, const void* weight
   qwa_status st = check_matmul_shape(ctx, m, n, k);
   if (st != QWA_OK) return st;
   if (m == 0) return QWA_OK;
-  if (!input || !weight || !output) return fail(ctx, QWA_ERR_INVALID_ARG, "NULL tensor pointer");
-  if (!aligned16(input) || !aligned16(weight) || !aligned16(output))
-    return fail(ctx, QWA_ERR_INVALID_ARG, "tensor pointers must be 16-byte aligned");
-  if ((st = ensure_encode(ctx)) != QWA_OK) return st;
-  const bool pair = gemm_pair(m);
-  CUtensorMap tm_a, tm_w, tm_out;
-  if ((st = make_map_2d(ctx, &tm_a, input, k, m, 128)) != QWA_OK) return st;
-  if ((st = make_map_2d(ctx, &tm_w, weight, k, n, kGemmWBoxRows(pair))) != QWA_OK) return st;
-  if ((st = make_map_2d(ctx, &tm_out, output, n / 2, m, 32)) != QWA_OK) return st;
-  QWA_CUDA(ctx, launch_gemm_glu(tm_a, tm_w, tm_out, static_cast<__half*>(output), m, n, k,
-                                ctx->d_status, pair, static_cast<cudaStream_t>(stream)));
-  return QWA_OK;
+  return run_matmul(ctx, input, weight, output, m, n, k, static_cast<cudaStream_t>(stream), true);
 }
 
 qwa_status qwa_matmul(qwa_ctx* ctx, const void* input, const void* weight, void* output, int m,
