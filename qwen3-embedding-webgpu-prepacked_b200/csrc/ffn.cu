@@ -2,7 +2,8 @@
 //
 // * SwiGLU of the FFN (swigluShader / SwiGLUKernel, src/webgpu/ops.ts:74-102):
 //     g = f32(combined[r, c]), u = f32(combined[r, width + c])
-//     out[r, c] = f16(g / (1 + exp(-g)) * u)
+//     out[r, c] = f16(silu(g) * u),  silu(g) = g / (1 + exp(-g)) in f32
+//   with the fast exponential and division (silu in internal.h)
 //   combined is the ffn_gate_up projection's output, gate columns first.
 //   One thread per 8 columns: two 16-byte loads, one 16-byte store.
 //
@@ -41,8 +42,8 @@ __global__ void __launch_bounds__(256)
   for (int k = 0; k < 4; ++k) {
     const float2 g = __half22float2(g2[k]);
     const float2 u = __half22float2(u2[k]);
-    const float s0 = g.x / (1.0f + expf(-g.x));
-    const float s1 = g.y / (1.0f + expf(-g.y));
+    const float s0 = silu(g.x);
+    const float s1 = silu(g.y);
     o2[k] = __floats2half2_rn(s0 * u.x, s1 * u.y);
   }
   __stcs(reinterpret_cast<uint4*>(out + r * width) + c, o);

@@ -376,16 +376,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // Fused SwiGLU (gate_up weight rows interleaved in 128-row blocks):
         // tile columns 0..127 are gate values g, 128..255 the up values u of
         // the same 128 outputs. Warp half h produces outputs [64h, 64h + 64):
-        // f16(g / (1 + exp(-g)) * u) with g and u first rounded to f16, as
-        // the unfused GEMM stores them and swiglu_kernel reads them.
+        // f16(silu(g) * u) with g and u first rounded to f16, as the unfused
+        // GEMM stores them and swiglu_kernel reads them.
         const int oc = nt * 128 + 64 * half;  // output column in [M, N / 2]
         auto glu_pack = [&](const uint32_t (&g)[32], const uint32_t (&u)[32], int i) {
           const float g0 = f16_round(__uint_as_float(g[2 * i]));
           const float g1 = f16_round(__uint_as_float(g[2 * i + 1]));
           const float u0 = f16_round(__uint_as_float(u[2 * i]));
           const float u1 = f16_round(__uint_as_float(u[2 * i + 1]));
-          const float s0 = g0 / (1.0f + expf(-g0));
-          const float s1 = g1 / (1.0f + expf(-g1));
+          const float s0 = silu(g0);
+          const float s1 = silu(g1);
           return pack_half2(s0 * u0, s1 * u1);
         };
         if constexpr (L::kTmaOut) {

@@ -156,6 +156,13 @@ cudaError_t launch_last_token_pool(const __half* hidden, int width, const int32_
 
 constexpr int kMaxDevices = 64;
 
+// silu(g) = g / (1 + exp(-g)) of the FFN's SwiGLU (ops.ts:74-102), with the
+// fast exponential and division intrinsics (errors of a few f32 ulp, far
+// below the f16 rounding of the product that follows). The unfused SwiGLU
+// kernel and the gate_up GEMM's fused epilogue share it, so both give the
+// same bits.
+__device__ __forceinline__ float silu(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
 // C[M,N] = A[M,K] W[N,K]^T, f16 in/out, f32 accumulate (tcgen05). tm_a: 2-D
 // map {K, M} box {64, 128}; tm_w: {K, N} box {64, kGemmWBoxRows(pair)};
 // 128-byte swizzle. N % 256 == 0, K % 64 == 0. pair: 256-row tiles on CTA
