@@ -405,8 +405,10 @@ def _graph_ms(torch, fn, reps=10):
 
 
 def run_gemm(args):
-    """Projection GEMM (tcgen05) against cuBLAS on the engine's shapes, and the
-    fused attn_qkv projection + Q/K norm + RoPE against GEMM + prologue. Inputs
+    """Projection GEMM (tcgen05) against cuBLAS on the engine's shapes, the
+    fused attn_qkv projection + Q/K norm + RoPE against GEMM + prologue, and
+    the gate_up projection with the SwiGLU in its epilogue against GEMM +
+    SwiGLU kernel. Inputs
     are larger than L2 except where stated; each number is a CUDA graph of 10
     launches timed with events."""
     import torch
@@ -445,6 +447,14 @@ def run_gemm(args):
                                                           v_out=v))
         gemm = _graph_ms(torch, lambda: mm.matmul(x, w, qkv))
         pro = _graph_ms(torch, lambda: attn.qk_norm_rope(qkv, qw, kw, cu, q_out=q, k_out=kk))
+        # ffn_gate_up with the SwiGLU in the epilogue against GEMM + SwiGLU kernel
+        wg = (torch.randn(6144, 1024, device="cuda") * 1024 ** -0.5).half()
+        wg_il = mm.interleave_gate_up(wg)
+        gu = torch.empty(rows, 6144, device="cuda", dtype=torch.half)
+        hid = torch.empty(rows, 3072, device="cuda", dtype=torch.half)
+        glu_fused = _graph_ms(torch, lambda: mm.matmul_swiglu(x, wg_il, hid))
+        glu_gemm = _graph_ms(torch, lambda: mm.matmul(x, wg, gu))
+        glu_act = _graph_ms(torch, lambda: pkg.ffn.swiglu(gu, 3072, hid))
     line = {
         "metric": "projection GEMM TFLOP/s (f16 in, f32 accumulate)", "unit": "TFLOP/s",
         "value": lines[0]["ours_tflops"], "n_gpus": 1, "dtype": "f16",
@@ -452,6 +462,10 @@ def run_gemm(args):
         "shapes": lines,
         "qkv_projection": {"rows": rows, "fused_ms": fused, "gemm_ms": gemm, "prologue_ms": pro,
                            "unfused_ms": gemm + pro, "speedup": (gemm + pro) / fused},
+        "gate_up_swiglu": {"rows": rows, "fused_ms": glu_fused, "gemm_ms": glu_gemm,
+                           "swiglu_ms": glu_act, "unfused_ms": glu_gemm + glu_act,
+                           "fused_tflops": 2.0 * rows * 6144 * 1024 / glu_fused / 1e9,
+                           "speedup": (glu_gemm + glu_act) / glu_fused},
         "timing": "CUDA graph of 10 launches per number, events", "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
