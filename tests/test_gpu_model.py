@@ -162,3 +162,23 @@ def test_multi_device_model_through_the_engine(pkg, cuda_dev, synthetic_model):
     for packing in ("varlen", "padded"):
         two = np.stack(asyncio.run(embed_all(multi, packing)))
         assert np.sum(one * two, axis=1).min() >= 0.9999
+
+
+def test_multi_device_model_on_two_gpus(pkg, cuda_dev, synthetic_model):
+    """The same split with the second replica on cuda:1 (skipped with one GPU):
+    weights, kernels and the packed batch of each share live on their own
+    device, and the gathered embeddings equal the single-device ones within
+    the batch-vs-single gate."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    parsed, model = synthetic_model
+    second = pkg.model.Qwen3EmbeddingModel(pkg.prepacked.PrepackedWeights(parsed, 1))
+    multi = pkg.model.MultiDeviceModel([model, second])
+    rng = np.random.default_rng(8)
+    lengths = [300, 700, 5, 150, 90, 1200]
+    ids = np.concatenate([rng.integers(0, 4095, size=n) for n in lengths]).astype(np.int64)
+    cu = [0] + np.cumsum(lengths).tolist()
+    two = multi.embed_packed(ids, cu)
+    d_ids = torch.from_numpy(ids.astype(np.int32)).cuda()
+    one = model.embed(d_ids, cu).cpu().numpy()
+    assert np.sum(one * two, axis=1).min() >= 0.9999
